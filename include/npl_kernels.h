@@ -1,0 +1,173 @@
+/*
+ * npl_kernels.h — device-level C ABI of libnpl_b200.so (prefix nplk_).
+ *
+ * These entry points replace the reference's microkernel / dispatch layer that
+ * the NPL operators call into:
+ *   mil_sgemm         composite/mkernel_interface/src/mil_gemm.cpp:210-330
+ *   k_dispatch_matmul composite/dispatch_kernel/src/k_kernel_dispatch.cpp:229-255
+ *   mil_reluf         composite/mkernel_interface/src/mil_vector.cpp:195-197
+ * and the per-operator CPU loops in advanced/neural_layer/src/*.cpp (cited per
+ * function below).
+ *
+ * Conventions:
+ *   - All tensor pointers are DEVICE pointers (cudaMalloc'd, managed, or a
+ *     torch tensor's data_ptr) of fp32 data unless stated otherwise.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Calls are asynchronous on that stream; nothing is synchronised.
+ *   - `workspace` is caller-provided device scratch of at least the size the
+ *     matching *_workspace_size() returns, 256-byte aligned.
+ *   - `status` is a device int the tcgen05 kernels set non-zero if one of their
+ *     bounded waits expired (the kernel then returns early instead of
+ *     hanging). It may be NULL; the library then uses its own per-device word,
+ *     read back with nplk_read_status().
+ *   - Return value: 0 on success, or a negative NPL_ERR_* code for invalid
+ *     arguments or CUDA launch errors.
+ */
+#ifndef NPL_B200_NPL_KERNELS_H_
+#define NPL_B200_NPL_KERNELS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef NPL_API
+#if defined(__GNUC__)
+#define NPL_API __attribute__((visibility("default")))
+#else
+#define NPL_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Optional epilogue activation codes (same values as npl_activation_t). */
+#define NPLK_ACT_NONE 0
+#define NPLK_ACT_RELU 1
+#define NPLK_ACT_LEAKY_RELU 7
+
+/* GEMM flags. */
+#define NPLK_GEMM_TF32_FAST 1u /* one TF32 pass instead of three (reported separately) */
+
+/* ---- dense contractions (tcgen05, 3xTF32) ---------------------------------- */
+
+/* Scratch bytes nplk_gemm needs for an M x N x K product (hi/lo operand splits). */
+NPL_API size_t nplk_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* C[M,N] = act(alpha * A[M,K] @ B[K,N] + beta * C + bias[N]), fp32 row-major
+ * with leading dimensions lda/ldb/ldc (elements). bias may be NULL. When
+ * beta == 0, C is not read. Replaces mil_sgemm -> cblas_sgemm
+ * (mil_gemm.cpp:290-316) on the npl_matmul path (npl_tensor_ops.cpp:217-311). */
+NPL_API int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float alpha, const float *A,
+              int64_t lda, const float *B, int64_t ldb, float beta, float *C, int64_t ldc,
+              const float *bias, int act, float act_alpha, unsigned flags, void *workspace,
+              size_t workspace_bytes, int *status);
+
+/* NCHW 2-D convolution geometry. Output is [N, Cout, Ho, Wo]. */
+typedef struct {
+  int64_t n, c_in, h, w;      /* input */
+  int64_t c_out, kh, kw;      /* weights [c_out, c_in, kh, kw] */
+  int64_t stride_h, stride_w; /* >= 1 */
+  int64_t pad_top, pad_left;  /* zero padding before the first row/column */
+  int64_t dil_h, dil_w;       /* >= 1 */
+  int64_t h_out, w_out;
+} nplk_conv_geom_t;
+
+/* Scratch bytes for nplk_conv2d_fused with this geometry (split weights and
+ * per-channel epilogue constants). */
+NPL_API size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g);
+
+/* out = act(BN(conv(x, w) + bias)) as one implicit-GEMM kernel: no im2col is
+ * materialised, BN (inference form gamma*(t-mean)/sqrt(var+eps)+beta, the
+ * formula of npl_activation_norm.cpp:389-398) and the activation run in the
+ * epilogue before the single HBM write. bias, and each of the BN arrays, may
+ * be NULL; with mean == NULL the BN step is skipped. act is an
+ * npl_activation_t value; act_alpha is the LeakyReLU slope. Replaces
+ * ExecuteConvDirect (npl_convolution.cpp:248-378) plus the BN / activation
+ * passes the reference leaves out (npl_convolution.cpp:116-126). */
+NPL_API int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x, const float *w,
+                      const float *bias, const float *bn_mean, const float *bn_var,
+                      const float *bn_gamma, const float *bn_beta, float bn_eps, int act,
+                      float act_alpha, float *out, void *workspace, size_t workspace_bytes,
+                      int *status);
+
+/* ---- bandwidth-bound primitives -------------------------------------------- */
+
+/* Depthwise conv, weights [C,1,kh,kw]; g->c_out must equal g->c_in. Dilation
+ * is ignored as in ExecuteDepthwiseConv (npl_convolution.cpp:904-991). */
+NPL_API int nplk_depthwise_conv2d(void *stream, const nplk_conv_geom_t *g, const float *x,
+                          const float *w, const float *bias, float *out);
+
+/* Inference batch norm over NCHW planes: y = gamma*(x-mean)*rsd + beta with
+ * rsd = 1/sqrt(var+eps) (npl_activation_norm.cpp:362-407). */
+NPL_API int nplk_batch_norm_infer(void *stream, int64_t n, int64_t c, int64_t hw, const float *x,
+                          float *y, const float *mean, const float *var, const float *gamma,
+                          const float *beta, float eps);
+
+/* Batch statistics for training-mode batch norm: per channel, the mean over
+ * N*HW and the biased variance (ComputeBatchStatistics,
+ * npl_activation_norm.cpp:524-552). mean/var are device arrays [c]. */
+NPL_API int nplk_batch_norm_stats(void *stream, int64_t n, int64_t c, int64_t hw, const float *x,
+                          float *mean, float *var);
+
+/* run = momentum*run + (1-momentum)*batch for mean and variance
+ * (npl_activation_norm.cpp:431-436). */
+NPL_API int nplk_bn_update_running(void *stream, int64_t c, float *run_mean, float *run_var,
+                           const float *mean, const float *var, float momentum);
+
+/* Elementwise activation of n elements (in place allowed). `scalar_semantics`
+ * selects the reference's scalar formulas (ExecuteActivationScalar,
+ * npl_activation_norm.cpp:186-230) instead of its vectorised path
+ * (ExecuteActivationVectorized :232-293); they differ for ReLU on NaN/-0. */
+NPL_API int nplk_activation(void *stream, int64_t n, const float *x, float *y, int act, float alpha,
+                    int scalar_semantics);
+
+/* Softmax over `axis_len` elements at stride `inner` for each of outer*inner
+ * lines (ExecuteSoftmaxAxis, npl_activation_norm.cpp:295-356). */
+NPL_API int nplk_softmax(void *stream, int64_t outer, int64_t axis_len, int64_t inner, const float *x,
+                 float *y);
+
+/* Layer norm of `rows` rows of `cols` elements, two-moment form
+ * (ExecuteLayerNormGeneric, npl_activation_norm.cpp:470-522). */
+NPL_API int nplk_layer_norm(void *stream, int64_t rows, int64_t cols, const float *x, float *y,
+                    const float *gamma, const float *beta, float eps);
+
+/* Max / average 2-D pooling over NCHW (ExecuteMaxPooling / ExecuteAvgPooling,
+ * npl_pooling.cpp:129-315). pool_type: 0 = max, 1 = average. */
+NPL_API int nplk_pool2d(void *stream, int64_t n, int64_t c, int64_t h, int64_t w, int64_t kh,
+                int64_t kw, int64_t sh, int64_t sw, int64_t ph, int64_t pw, int64_t h_out,
+                int64_t w_out, int pool_type, int count_include_pad, const float *x, float *y);
+
+/* Mean over each of `planes` contiguous planes of `hw` elements
+ * (ExecuteGlobalAvgPooling, npl_pooling.cpp:317-385). */
+NPL_API int nplk_global_avg_pool(void *stream, int64_t planes, int64_t hw, const float *x, float *y);
+
+/* Elementwise binary ops over n elements: op 0 = add, 1 = mul.
+ * b_mode: 0 = same shape, 1 = b is a scalar, 2 = a is a scalar,
+ * 3 = b is per-channel [C] over NCHW planes of `inner` elements. */
+NPL_API int nplk_binary(void *stream, int op, int64_t n, const float *a, const float *b, float *c,
+                int b_mode, int64_t channels, int64_t inner);
+
+/* ---- multi-GPU helpers ------------------------------------------------------ */
+
+/* Column-shard relayout after an all-gather: src is [g][rows][cols_per_shard]
+ * (shard-major, as an all-gather of per-rank C blocks delivers it); dst is
+ * row-major [rows][g*cols_per_shard]. */
+NPL_API int nplk_colshard_relayout(void *stream, int64_t g, int64_t rows, int64_t cols_per_shard,
+                           const float *src, float *dst);
+
+/* ---- status ----------------------------------------------------------------- */
+
+/* Reads (and clears) the library's per-device kernel status word; 0 = ok.
+ * Synchronises `stream`. */
+NPL_API int nplk_read_status(void *stream);
+
+/* Number of library kernels launched on this thread since the last call
+ * (resets the counter). */
+NPL_API uint64_t nplk_take_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NPL_B200_NPL_KERNELS_H_ */

@@ -1,0 +1,468 @@
+// K2: NCHW 2-D convolution as an implicit GEMM on the sm_100a tensor cores
+// (3xTF32), with bias, inference batch norm and activation in the epilogue.
+//
+// GEMM view: D[m][co] = sum_k A[m][k] * W'[co][k]
+//   m  = (n, oh, ow)           output pixel, M = N*Ho*Wo
+//   k  = (kh, kw, ci)          tap-major reduction index, K = KH*KW*Cin
+//   A[m][k] = x[n][ci][oh*sh - pt + kh*dh][ow*sw - pl + kw*dw]  (0 outside)
+//   W'[co][k] = w[co][ci][kh][kw]
+// Reference semantics: ExecuteConvDirect (advanced/neural_layer/src/
+// npl_convolution.cpp:248-378) accumulates the same products in fp32; the
+// epilogue then applies bias (:344-367), batch norm in the inference form of
+// ExecuteBatchNormInference (npl_activation_norm.cpp:389-398) and the
+// activation, i.e. what npl_conv2d_bn_activation is specified to compute
+// (the reference itself stops after the conv, npl_convolution.cpp:116-126).
+//
+// No im2col matrix is materialised. Per persistent CTA (416 threads):
+//   warps 0-7   gather A: each thread owns one pixel row and 16 of the 32
+//               k-columns of a stage, loads them straight from NCHW global
+//               memory (coalesced along ow), splits each value into tf32
+//               hi/lo and writes both into 128-byte-swizzled shared memory;
+//               thread 0 also TMA-loads the matching [W'_hi; W'_lo] slab;
+//   warp 8      issues tcgen05.mma: MMA(A_hi, [W_hi; W_lo]) with N = 2*BNC and
+//               MMA(A_lo, W_hi) with N = BNC into a TMEM accumulator;
+//   warps 9-12  epilogue: out = act(BN(D[:, :BNC] + D[:, BNC:] + bias)),
+//               one coalesced HBM write per output element.
+// The weights are prepared by conv_prep_kernel (permute to tap-major, split,
+// zero-pad) together with the per-channel epilogue constants.
+#include <cuda_runtime.h>
+
+#include "nplk_device.cuh"
+#include "nplk_host.h"
+#include "ptx_sm100.cuh"
+
+namespace nplk {
+
+constexpr int kConvBM = 128;
+constexpr int kConvBK = 32;
+constexpr int kConvProducerWarps = 8;
+constexpr int kConvMmaWarp = kConvProducerWarps;  // warps after it: epilogue
+constexpr int kConvThreads = (kConvProducerWarps + 1 + 4) * 32;
+
+template <int BNC>
+struct ConvTraits {
+  static constexpr int kStages = BNC == 64 ? 4 : 3;
+  static constexpr int kAStageBytes = 2 * kConvBM * kConvBK * 4;  // hi + lo: 32 KB
+  static constexpr int kBStageBytes = 2 * BNC * kConvBK * 4;
+  static constexpr int kAccCols = 2 * BNC;
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kSmemBytes = 1024 + kStages * (kAStageBytes + kBStageBytes) + 256;
+};
+
+// Per-channel epilogue constants, [5][cout_pad]: bias, mean, gamma, beta,
+// 1/sqrt(var+eps).
+enum { kEpBias = 0, kEpMean = 1, kEpGamma = 2, kEpBeta = 3, kEpInvStd = 4, kEpCount = 5 };
+
+struct ConvParams {
+  const float *x;
+  float *y;
+  int C, H, W, Cout, KH, KW, sh, sw, pt, pl, dh, dw, Ho, Wo;
+  int64_t HW, HoWo, CHW;
+  int M;
+  int K, k_blocks, m_blocks, n_blocks;
+  const float *ep;
+  int cout_pad;
+  int has_bn, act;
+  float act_alpha;
+  int *status;
+};
+
+template <int BNC>
+__global__ void __launch_bounds__(kConvThreads, 1)
+    conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
+  using T = ConvTraits<BNC>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem_a = smem;
+  uint8_t *smem_b = smem + T::kStages * T::kAStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem_b + T::kStages * T::kBStageBytes);
+  uint64_t *empty = full + T::kStages;
+  uint64_t *acc_full = empty + T::kStages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::kStages; ++s) {
+      mbar_init(&full[s], kConvProducerWarps + 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_w);
+  }
+  if (warp == kConvMmaWarp) {
+    tmem_alloc(tmem_slot, T::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (warp < kConvProducerWarps) {
+    // ---------------- A gather + weight TMA ----------------
+    const int row = threadIdx.x & (kConvBM - 1);
+    const int half = threadIdx.x >> 7;  // which 16 of the 32 k-columns
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int mb = tile / p.n_blocks;
+      const int nb = tile - mb * p.n_blocks;
+      const int m = mb * kConvBM + row;
+      const bool valid = m < p.M;
+      int n = 0, oh = 0, ow = 0;
+      if (valid) {
+        n = m / static_cast<int>(p.HoWo);
+        const int pix = m - n * static_cast<int>(p.HoWo);
+        oh = pix / p.Wo;
+        ow = pix - oh * p.Wo;
+      }
+      const int ih0 = oh * p.sh - p.pt;
+      const int iw0 = ow * p.sw - p.pl;
+      const float *xb = p.x + static_cast<int64_t>(n) * p.CHW;
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutProducer))
+          goto producer_done;
+        if (threadIdx.x == 0) {
+          mbar_arrive_expect_tx(&full[stage], T::kBStageBytes);
+          tma_load_2d(&map_w, &full[stage], smem_b + stage * T::kBStageBytes, kb * kConvBK,
+                      nb * 2 * BNC);
+        }
+        // Decode the first of this thread's 16 k indices, then walk them.
+        int k = kb * kConvBK + half * 16;
+        int tap = k / p.C;
+        int ci = k - tap * p.C;
+        int kh = tap / p.KW;
+        int kw = tap - kh * p.KW;
+        int ih = ih0 + kh * p.dh;
+        int iw = iw0 + kw * p.dw;
+        bool ok = valid && kh < p.KH && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                  static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+        const float *ptr = xb + static_cast<int64_t>(ci) * p.HW +
+                           static_cast<int64_t>(ih) * p.W + iw;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v[j] = ok ? __ldg(ptr) : 0.0f;
+          ptr += p.HW;
+          if (++ci == p.C) {
+            ci = 0;
+            if (++kw == p.KW) {
+              kw = 0;
+              ++kh;
+            }
+            ih = ih0 + kh * p.dh;
+            iw = iw0 + kw * p.dw;
+            ok = valid && kh < p.KH &&
+                 static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                 static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+            ptr = xb + static_cast<int64_t>(ih) * p.W + iw;
+          }
+        }
+        uint8_t *a_hi = smem_a + stage * T::kAStageBytes;
+        uint8_t *a_lo = a_hi + kConvBM * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float4 hi, lo;
+          tf32_split(v[4 * c + 0], hi.x, lo.x);
+          tf32_split(v[4 * c + 1], hi.y, lo.y);
+          tf32_split(v[4 * c + 2], hi.z, lo.z);
+          tf32_split(v[4 * c + 3], hi.w, lo.w);
+          const uint32_t off = sw128_offset(row, half * 4 + c);
+          *reinterpret_cast<float4 *>(a_hi + off) = hi;
+          *reinterpret_cast<float4 *>(a_lo + off) = lo;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[stage]);
+        if (++stage == T::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  producer_done:;
+  } else if (warp == kConvMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_2n = umma_idesc_tf32(kConvBM, 2 * BNC);
+      const uint32_t idesc_n = umma_idesc_tf32(kConvBM, BNC);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutAccFree))
+          break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * T::kAccCols;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma))
+            goto mma_done;
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(smem_a + stage * T::kAStageBytes);
+          const uint32_t b_addr = smem_u32(smem_b + stage * T::kBStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kConvBK / 8; ++kk) {
+            const uint64_t a_hi = umma_desc_sw128(a_addr + kk * 32);
+            const uint64_t a_lo = umma_desc_sw128(a_addr + kConvBM * 128 + kk * 32);
+            const uint64_t b = umma_desc_sw128(b_addr + kk * 32);
+            mma_tf32_ss(d_tmem, a_hi, b, idesc_2n, (kb > 0 || kk > 0) ? 1u : 0u);
+            mma_tf32_ss(d_tmem, a_lo, b, idesc_n, 1u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == T::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        mma_commit(&acc_full[acc]);
+      }
+    mma_done:;
+    }
+  } else {
+    // ---------------- epilogue (warps 9..12) ----------------
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const float *ep_bias = p.ep + kEpBias * p.cout_pad;
+    const float *ep_mean = p.ep + kEpMean * p.cout_pad;
+    const float *ep_gamma = p.ep + kEpGamma * p.cout_pad;
+    const float *ep_beta = p.ep + kEpBeta * p.cout_pad;
+    const float *ep_inv = p.ep + kEpInvStd * p.cout_pad;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after_sync();
+      const int mb = tile / p.n_blocks;
+      const int nb = tile - mb * p.n_blocks;
+      const int m = mb * kConvBM + row;
+      const bool valid = m < p.M;
+      int n = 0, pix = 0;
+      if (valid) {
+        n = m / static_cast<int>(p.HoWo);
+        pix = m - n * static_cast<int>(p.HoWo);
+      }
+      float *yb = p.y + static_cast<int64_t>(n) * p.Cout * p.HoWo + pix;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * T::kAccCols);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BNC; c0 += 32) {
+        uint32_t v[32], w[32];
+        tmem_ld32(t_row + c0, v);
+        tmem_ld32(t_row + BNC + c0, w);
+        tmem_wait_ld2(v, w);
+        const int co0 = nb * BNC + c0;
+        if (valid) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int co = co0 + j;
+            if (co < p.Cout) {
+              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + ep_bias[co];
+              if (p.has_bn) t = ep_gamma[co] * (t - ep_mean[co]) * ep_inv[co] + ep_beta[co];
+              yb[static_cast<int64_t>(co) * p.HoWo] = apply_act(t, p.act, p.act_alpha);
+            }
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == kConvMmaWarp) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+}
+
+// Weight preparation: w[co][ci][kh][kw] -> tap-major, tf32-split, blocked
+// [n_blocks][2][BNC][kp] (zero padded), plus the epilogue constants.
+__global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, int KH, int KW,
+                                 int kp, int bnc, float *__restrict__ wsplit,
+                                 int64_t wsplit_elems, const float *bias, const float *mean,
+                                 const float *var, const float *gamma, const float *beta,
+                                 float eps, float *__restrict__ ep, int cout_pad) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int K = C * KH * KW;
+  // One thread per (row, k) of the hi part; it also writes the lo part.
+  const int64_t half_elems = wsplit_elems / 2;
+  for (int64_t i = tid; i < half_elems; i += stride) {
+    const int64_t rowg = i / kp;  // global padded output-channel row
+    const int k = static_cast<int>(i - rowg * kp);
+    const int co = static_cast<int>(rowg);
+    float x = 0.0f;
+    if (co < Cout && k < K) {
+      const int tap = k / C;
+      const int ci = k - tap * C;
+      const int kh = tap / KW;
+      const int kw = tap - kh * KW;
+      x = w[((static_cast<int64_t>(co) * C + ci) * KH + kh) * KW + kw];
+    }
+    float hi, lo;
+    tf32_split(x, hi, lo);
+    const int blk = co / bnc;
+    const int rr = co - blk * bnc;
+    float *d = wsplit + ((static_cast<int64_t>(blk) * 2) * bnc + rr) * kp + k;
+    d[0] = hi;
+    d[static_cast<int64_t>(bnc) * kp] = lo;
+  }
+  for (int64_t c = tid; c < cout_pad; c += stride) {
+    const bool in = c < Cout;
+    ep[kEpBias * cout_pad + c] = (in && bias) ? bias[c] : 0.0f;
+    ep[kEpMean * cout_pad + c] = (in && mean) ? mean[c] : 0.0f;
+    ep[kEpGamma * cout_pad + c] = (in && gamma) ? gamma[c] : 1.0f;
+    ep[kEpBeta * cout_pad + c] = (in && beta) ? beta[c] : 0.0f;
+    ep[kEpInvStd * cout_pad + c] = (in && var) ? 1.0f / sqrtf(var[c] + eps) : 1.0f;
+  }
+}
+
+namespace {
+
+struct ConvPlan {
+  int bnc;
+  int64_t kp, n_blocks, cout_pad;
+  size_t w_bytes, ep_bytes;
+};
+
+ConvPlan plan_conv(const nplk_conv_geom_t *g) {
+  ConvPlan c{};
+  c.bnc = g->c_out <= 64 ? 64 : 128;
+  const int64_t K = g->c_in * g->kh * g->kw;
+  c.kp = ceil_div(K, kConvBK) * kConvBK;
+  c.n_blocks = ceil_div(g->c_out, c.bnc);
+  c.cout_pad = c.n_blocks * c.bnc;
+  c.w_bytes = align_up(static_cast<size_t>(c.cout_pad) * 2 * c.kp * 4, 256);
+  c.ep_bytes = align_up(static_cast<size_t>(kEpCount) * c.cout_pad * 4, 256);
+  return c;
+}
+
+template <int BNC>
+int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
+  using T = ConvTraits<BNC>;
+  CUtensorMap map_w;
+  int rc = encode_tmap_2d_f32_sw128(&map_w, wsplit, c.kp, c.n_blocks * 2 * BNC, c.kp * 4,
+                                    kConvBK, 2 * BNC);
+  if (rc) return rc;
+  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC>),
+                           T::kSmemBytes);
+  if (rc) return rc;
+  const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  conv_igemm_3xtf32_kernel<BNC><<<grid, kConvThreads, T::kSmemBytes, s>>>(map_w, prm);
+  count_launch();
+  return launch_result();
+}
+
+}  // namespace
+
+int validate_conv_geom(const nplk_conv_geom_t *g) {
+  if (!g) return kErrInvalidArg;
+  if (g->n <= 0 || g->c_in <= 0 || g->h <= 0 || g->w <= 0 || g->c_out <= 0 || g->kh <= 0 ||
+      g->kw <= 0 || g->stride_h <= 0 || g->stride_w <= 0 || g->dil_h <= 0 || g->dil_w <= 0 ||
+      g->h_out <= 0 || g->w_out <= 0 || g->pad_top < 0 || g->pad_left < 0)
+    return kErrInvalidArg;
+  // 32-bit index arithmetic inside the kernels.
+  const int64_t lim = int64_t(1) << 31;
+  if (g->n * g->h_out * g->w_out >= lim || g->n * g->c_in * g->h * g->w >= (int64_t(1) << 40) ||
+      g->c_in * g->kh * g->kw >= lim / 64 || g->h >= lim || g->w >= lim ||
+      g->h_out * g->w_out >= lim)
+    return kErrUnsupported;
+  return kOk;
+}
+
+}  // namespace nplk
+
+using namespace nplk;
+
+extern "C" size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g) {
+  if (validate_conv_geom(g) != kOk) return 0;
+  const ConvPlan c = plan_conv(g);
+  return c.w_bytes + c.ep_bytes;
+}
+
+extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                 const float *w, const float *bias, const float *bn_mean,
+                                 const float *bn_var, const float *bn_gamma,
+                                 const float *bn_beta, float bn_eps, int act, float act_alpha,
+                                 float *out, void *workspace, size_t workspace_bytes,
+                                 int *status) {
+  int rc = validate_conv_geom(g);
+  if (rc) return rc;
+  if (!x || !w || !out) return kErrInvalidArg;
+  const ConvPlan c = plan_conv(g);
+  if (!workspace || workspace_bytes < c.w_bytes + c.ep_bytes ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return kErrInvalidArg;
+  if (!status) status = device_status_word();
+  if (!status) return kErrInternal;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float *wsplit = static_cast<float *>(workspace);
+  float *ep = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + c.w_bytes);
+
+  const int64_t wsplit_elems = c.cout_pad * 2 * c.kp;
+  {
+    const int threads = 256;
+    int64_t blocks = ceil_div(wsplit_elems / 2, threads);
+    if (blocks > 4096) blocks = 4096;
+    conv_prep_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+        w, static_cast<int>(g->c_out), static_cast<int>(g->c_in), static_cast<int>(g->kh),
+        static_cast<int>(g->kw), static_cast<int>(c.kp), c.bnc, wsplit, wsplit_elems, bias,
+        bn_mean, bn_var, bn_gamma, bn_beta, bn_eps, ep, static_cast<int>(c.cout_pad));
+    count_launch();
+    rc = launch_result();
+    if (rc) return rc;
+  }
+
+  ConvParams prm{};
+  prm.x = x;
+  prm.y = out;
+  prm.C = static_cast<int>(g->c_in);
+  prm.H = static_cast<int>(g->h);
+  prm.W = static_cast<int>(g->w);
+  prm.Cout = static_cast<int>(g->c_out);
+  prm.KH = static_cast<int>(g->kh);
+  prm.KW = static_cast<int>(g->kw);
+  prm.sh = static_cast<int>(g->stride_h);
+  prm.sw = static_cast<int>(g->stride_w);
+  prm.pt = static_cast<int>(g->pad_top);
+  prm.pl = static_cast<int>(g->pad_left);
+  prm.dh = static_cast<int>(g->dil_h);
+  prm.dw = static_cast<int>(g->dil_w);
+  prm.Ho = static_cast<int>(g->h_out);
+  prm.Wo = static_cast<int>(g->w_out);
+  prm.HW = g->h * g->w;
+  prm.HoWo = g->h_out * g->w_out;
+  prm.CHW = g->c_in * g->h * g->w;
+  prm.M = static_cast<int>(g->n * g->h_out * g->w_out);
+  prm.K = static_cast<int>(g->c_in * g->kh * g->kw);
+  prm.k_blocks = static_cast<int>(c.kp / kConvBK);
+  prm.m_blocks = static_cast<int>(ceil_div(prm.M, kConvBM));
+  prm.n_blocks = static_cast<int>(c.n_blocks);
+  prm.ep = ep;
+  prm.cout_pad = static_cast<int>(c.cout_pad);
+  prm.has_bn = bn_mean != nullptr ? 1 : 0;
+  prm.act = act;
+  prm.act_alpha = act_alpha;
+  prm.status = status;
+  if (c.bnc == 64) return launch_conv<64>(s, c, wsplit, prm);
+  return launch_conv<128>(s, c, wsplit, prm);
+}

@@ -1,0 +1,379 @@
+// K1: fp32 GEMM on the sm_100a tensor cores with 3xTF32 split precision.
+//
+// C = act(alpha * A @ B + beta * C + bias), the arithmetic the reference
+// obtains from cblas_sgemm behind npl_matmul (advanced/neural_layer/src/
+// npl_tensor_ops.cpp:217-311 -> composite/mkernel_interface/src/
+// mil_gemm.cpp:290-316).
+//
+// Pipeline (one persistent CTA per SM, 192 threads):
+//   1. split kernels (split_tf32.cu) write A and B^T as tf32 hi/lo pairs in a
+//      blocked, zero-padded, K-major layout:
+//        A': [m_blocks][2][128][Kp]   (hi rows, then lo rows, per 128-row block)
+//        B': [n_blocks][2][BN][Kp]    (B transposed: rows are output columns)
+//   2. warp 0 streams 32-wide K slabs of A' and B' into a ring of shared-memory
+//      stages with TMA (128-byte swizzle, no multicast);
+//   3. warp 1 issues tcgen05.mma kind::tf32 into a TMEM accumulator of 2*BN
+//      columns: MMA(A_hi, [B_hi;B_lo]) with N = 2*BN gives A_hi*B_hi in the
+//      first BN columns and A_hi*B_lo in the second; MMA(A_lo, B_hi) with
+//      N = BN adds A_lo*B_hi into the first BN columns;
+//   4. warps 2-5 drain the (double-buffered) accumulator: C = alpha*(D[:, :BN]
+//      + D[:, BN:]) + beta*C + bias, activation, store.
+#include <cuda_runtime.h>
+
+#include "nplk_device.cuh"
+#include "nplk_host.h"
+#include "ptx_sm100.cuh"
+
+namespace nplk {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 32;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmTraits {
+  static constexpr int kStages = BN == 128 ? 3 : 4;
+  static constexpr int kAStageBytes = 2 * kGemmBM * kGemmBK * 4;  // hi + lo, 32 KB
+  static constexpr int kBStageBytes = 2 * BN * kGemmBK * 4;       // hi + lo
+  static constexpr int kStageBytes = kAStageBytes + kBStageBytes;
+  static constexpr int kAccCols = 2 * BN;
+  static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+};
+
+struct GemmParams {
+  int M, N, K;
+  int m_blocks, n_blocks, k_blocks;
+  float alpha, beta;
+  float *C;
+  int64_t ldc;
+  const float *bias;
+  int act;
+  float act_alpha;
+  int one_pass;
+  int *status;
+};
+
+// Tile order: groups of 8 M-blocks sweep all N-blocks, so the CTAs resident at
+// one time share A row-blocks and B column-blocks in L2.
+__device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_blocks, int &mb,
+                                                 int &nb) {
+  constexpr int kGroup = 8;
+  const int per_group = kGroup * n_blocks;
+  const int group = tile / per_group;
+  const int first_m = group * kGroup;
+  const int gsize = min(m_blocks - first_m, kGroup);
+  const int local = tile - group * per_group;
+  mb = first_m + local % gsize;
+  nb = local / gsize;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+  using T = GemmTraits<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem_a = smem;
+  uint8_t *smem_b = smem + T::kStages * T::kAStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem_b + T::kStages * T::kBStageBytes);
+  uint64_t *empty = full + T::kStages;
+  uint64_t *acc_full = empty + T::kStages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, T::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                         kStatusTimeoutProducer))
+            goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], T::kStageBytes);
+          tma_load_2d(&map_a, &full[stage], smem_a + stage * T::kAStageBytes, kb * kGemmBK,
+                      mb * 2 * kGemmBM);
+          tma_load_2d(&map_b, &full[stage], smem_b + stage * T::kBStageBytes, kb * kGemmBK,
+                      nb * 2 * BN);
+          if (++stage == T::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_2n = umma_idesc_tf32(kGemmBM, 2 * BN);
+      const uint32_t idesc_n = umma_idesc_tf32(kGemmBM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutAccFree))
+          break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * T::kAccCols;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma))
+            goto mma_done;
+          tc_fence_after_sync();
+          const uint32_t a_addr = smem_u32(smem_a + stage * T::kAStageBytes);
+          const uint32_t b_addr = smem_u32(smem_b + stage * T::kBStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 8; ++kk) {
+            const uint64_t a_hi = umma_desc_sw128(a_addr + kk * 32);
+            const uint64_t a_lo = umma_desc_sw128(a_addr + kGemmBM * 128 + kk * 32);
+            const uint64_t b = umma_desc_sw128(b_addr + kk * 32);
+            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+            if (p.one_pass) {
+              mma_tf32_ss(d_tmem, a_hi, b, idesc_n, accum);
+            } else {
+              mma_tf32_ss(d_tmem, a_hi, b, idesc_2n, accum);
+              mma_tf32_ss(d_tmem, a_lo, b, idesc_n, 1u);
+            }
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == T::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        mma_commit(&acc_full[acc]);
+      }
+    mma_done:;
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
+                        ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after_sync();
+      int mb, nb;
+      gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+      const int r = mb * kGemmBM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * T::kAccCols);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32], w[32];
+        tmem_ld32(t_row + c0, v);
+        if (!p.one_pass) {
+          tmem_ld32(t_row + BN + c0, w);
+          tmem_wait_ld2(v, w);
+        } else {
+          tmem_wait_ld(v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = 0u;
+        }
+        const int col0 = nb * BN + c0;
+        if (r < p.M && col0 < p.N) {
+          float *crow = p.C + static_cast<int64_t>(r) * p.ldc;
+          float out[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            out[j] = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
+          if (vec_ok && col0 + 32 <= p.N) {
+            float4 *dst = reinterpret_cast<float4 *>(crow + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 o = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+              if (p.beta != 0.0f) {
+                const float4 c = dst[q];
+                o.x += p.beta * c.x;
+                o.y += p.beta * c.y;
+                o.z += p.beta * c.z;
+                o.w += p.beta * c.w;
+              }
+              if (p.bias) {
+                o.x += p.bias[col0 + 4 * q];
+                o.y += p.bias[col0 + 4 * q + 1];
+                o.z += p.bias[col0 + 4 * q + 2];
+                o.w += p.bias[col0 + 4 * q + 3];
+              }
+              o.x = apply_act(o.x, p.act, p.act_alpha);
+              o.y = apply_act(o.y, p.act, p.act_alpha);
+              o.z = apply_act(o.z, p.act, p.act_alpha);
+              o.w = apply_act(o.w, p.act, p.act_alpha);
+              dst[q] = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = col0 + j;
+              if (col < p.N) {
+                float o = out[j];
+                if (p.beta != 0.0f) o += p.beta * crow[col];
+                if (p.bias) o += p.bias[col];
+                crow[col] = apply_act(o, p.act, p.act_alpha);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host launcher
+// ---------------------------------------------------------------------------
+namespace {
+
+struct GemmPlan {
+  int bn;
+  int64_t m_blocks, n_blocks, kp;
+  size_t a_bytes, b_bytes;
+};
+
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K) {
+  GemmPlan g{};
+  g.m_blocks = ceil_div(M, kGemmBM);
+  g.kp = ceil_div(K, kGemmBK) * kGemmBK;
+  const int64_t tiles128 = g.m_blocks * ceil_div(N, 128);
+  g.bn = (tiles128 >= sm_count()) ? 128 : 64;
+  g.n_blocks = ceil_div(N, g.bn);
+  g.a_bytes = align_up(static_cast<size_t>(g.m_blocks) * 2 * kGemmBM * g.kp * 4, 256);
+  g.b_bytes = align_up(static_cast<size_t>(g.n_blocks) * 2 * g.bn * g.kp * 4, 256);
+  return g;
+}
+
+template <int BN>
+int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
+                const float *b_split, GemmParams prm) {
+  using T = GemmTraits<BN>;
+  CUtensorMap map_a, map_b;
+  int rc = encode_tmap_2d_f32_sw128(&map_a, a_split, g.kp, g.m_blocks * 2 * kGemmBM, g.kp * 4,
+                                    kGemmBK, 2 * kGemmBM);
+  if (rc) return rc;
+  rc = encode_tmap_2d_f32_sw128(&map_b, b_split, g.kp, g.n_blocks * 2 * BN, g.kp * 4, kGemmBK,
+                                2 * BN);
+  if (rc) return rc;
+  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN>),
+                          T::kSmemBytes);
+  if (rc) return rc;
+  const int64_t tiles = g.m_blocks * g.n_blocks;
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  gemm_3xtf32_kernel<BN><<<grid, kGemmThreads, T::kSmemBytes, stream>>>(map_a, map_b, prm);
+  count_launch();
+  return launch_result();
+}
+
+}  // namespace
+
+// Split launchers (split_tf32.cu).
+int launch_split_rows(cudaStream_t s, const float *src, int64_t rows, int64_t cols, int64_t ld,
+                      int64_t col_offset, float *dst, int row_block, int64_t kp,
+                      int64_t rows_pad);
+int launch_split_transpose(cudaStream_t s, const float *src, int64_t krows, int64_t ncols,
+                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad);
+
+}  // namespace nplk
+
+using namespace nplk;
+
+extern "C" size_t nplk_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const GemmPlan g = plan_gemm(M, N, K);
+  return g.a_bytes + g.b_bytes;
+}
+
+extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float alpha,
+                         const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                         float *C, int64_t ldc, const float *bias, int act, float act_alpha,
+                         unsigned flags, void *workspace, size_t workspace_bytes,
+                         int *status) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return kErrInvalidArg;
+  if (lda < K || ldb < N || ldc < N) return kErrInvalidArg;
+  if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
+    return kErrUnsupported;
+  const GemmPlan g = plan_gemm(M, N, K);
+  if (!workspace || workspace_bytes < g.a_bytes + g.b_bytes) return kErrInvalidArg;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kErrInvalidArg;
+  if (!status) status = device_status_word();
+  if (!status) return kErrInternal;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float *a_split = static_cast<float *>(workspace);
+  float *b_split = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + g.a_bytes);
+
+  int rc = launch_split_rows(s, A, M, K, lda, 0, a_split, kGemmBM, g.kp, g.m_blocks * kGemmBM);
+  if (rc) return rc;
+  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn);
+  if (rc) return rc;
+
+  GemmParams prm{};
+  prm.M = static_cast<int>(M);
+  prm.N = static_cast<int>(N);
+  prm.K = static_cast<int>(K);
+  prm.m_blocks = static_cast<int>(g.m_blocks);
+  prm.n_blocks = static_cast<int>(g.n_blocks);
+  prm.k_blocks = static_cast<int>(g.kp / kGemmBK);
+  prm.alpha = alpha;
+  prm.beta = beta;
+  prm.C = C;
+  prm.ldc = ldc;
+  prm.bias = bias;
+  prm.act = act;
+  prm.act_alpha = act_alpha;
+  prm.one_pass = (flags & NPLK_GEMM_TF32_FAST) ? 1 : 0;
+  prm.status = status;
+  if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm);
+  return launch_gemm<64>(s, g, a_split, b_split, prm);
+}

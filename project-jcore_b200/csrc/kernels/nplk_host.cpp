@@ -1,0 +1,131 @@
+// Host-side helpers for the kernel launchers (see nplk_host.h).
+#include "nplk_host.h"
+
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
+
+namespace nplk {
+
+int map_cuda_error(cudaError_t e) {
+  switch (e) {
+    case cudaSuccess:
+      return kOk;
+    case cudaErrorMemoryAllocation:
+      return kErrOom;
+    case cudaErrorInvalidValue:
+    case cudaErrorInvalidDevicePointer:
+      return kErrInvalidArg;
+    default:
+      return kErrInternal;
+  }
+}
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::once_flag g_sm_once[kMaxDevices];
+int g_sm_count[kMaxDevices];
+std::mutex g_status_mu;
+int *g_status[kMaxDevices];
+thread_local uint64_t t_launches = 0;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  std::call_once(g_sm_once[dev], [dev] {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sm_count[dev] = n > 0 ? n : 148;
+  });
+  return g_sm_count[dev];
+}
+
+int *device_status_word() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  if (!g_status[dev]) {
+    int *p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(int)) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    g_status[dev] = p;
+  }
+  return g_status[dev];
+}
+
+void count_launch(uint64_t n) { t_launches += n; }
+
+int launch_result() { return map_cuda_error(cudaGetLastError()); }
+
+int ensure_dynamic_smem(const void *func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void *>> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kErrInternal;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({dev, func})) return kOk;
+  cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return map_cuda_error(e);
+  done.insert({dev, func});
+  return kOk;
+}
+
+int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
+                             uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
+                             uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return kErrInternal;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_pitch_bytes & 15u) != 0)
+    return kErrInvalidArg;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInternal;
+}
+
+}  // namespace nplk
+
+extern "C" int nplk_read_status(void *stream) {
+  int *w = nplk::device_status_word();
+  if (!w) return nplk::kErrInternal;
+  int v = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+    return nplk::kErrInternal;
+  if (cudaMemsetAsync(w, 0, sizeof(int), s) != cudaSuccess) return nplk::kErrInternal;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return nplk::kErrInternal;
+  return v;
+}
+
+extern "C" uint64_t nplk_take_launch_count(void) {
+  uint64_t n = nplk::t_launches;
+  nplk::t_launches = 0;
+  return n;
+}

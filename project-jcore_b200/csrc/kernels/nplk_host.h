@@ -1,0 +1,51 @@
+// Host-side helpers shared by the kernel launchers: CUDA error mapping,
+// per-device properties, TMA descriptor encoding, the library status word and
+// the launch counter.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "npl_kernels.h"
+
+namespace nplk {
+
+// NPL error codes (mirrors include/neural_primitives.h).
+constexpr int kOk = 0;
+constexpr int kErrInvalidArg = -2;
+constexpr int kErrNoMemory = -3;
+constexpr int kErrInternal = -4;
+constexpr int kErrUnsupported = -5;
+constexpr int kErrOom = -7;
+
+int map_cuda_error(cudaError_t e);
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Device status word of the current device (allocated on first use).
+int *device_status_word();
+
+// Counts one library kernel launch on the calling thread.
+void count_launch(uint64_t n = 1);
+
+// Checks the last launch and maps the error.
+int launch_result();
+
+// Raises a kernel's dynamic shared-memory limit on the current device (once
+// per device and function).
+int ensure_dynamic_smem(const void *func, int bytes);
+
+// 2-D fp32 tensor map: dims {inner, outer} elements, row pitch in bytes,
+// box {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds.
+int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
+                             uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
+                             uint32_t box_outer);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace nplk
