@@ -1,0 +1,479 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 NPL backend on its headline workload.
+
+Workload (one "step"): npl_conv2d_bn_activation on the ResNet-style 3x3 layer
+N=32, C_in=64, H=W=56, C_out=64, stride 1, pad 1, no bias, inference BN
+(gamma U[0.5,1.5], beta U[-0.1,0.1], mean N(0,0.1), var U[0.5,1.5], eps 1e-5),
+ReLU; input U[0,1], weights N(0, sqrt(2/576)). Synthetic seeded inputs.
+A step is the full operator: weight preparation (tf32 split + BN constants)
+plus the fused implicit-GEMM conv kernel. At N GPUs every rank runs its own
+batch of 32 (batch-sharded data parallelism, no collective): weak scaling.
+
+Reported (one JSON line on rank 0):
+  value     whole-job TFLOP/s (2*N*Cout*Cin*Ho*Wo*9 per batch) with inputs
+            resident in HBM, timed with CUDA events per step, L2 flushed
+            between steps outside the timed events, max over ranks;
+  e2e       the same metric through the public C ABI with pinned host
+            buffers (host->device input copies and device->host output copy
+            inside every step);
+  roofline  the conv kernel against the 3xTF32 tensor-core roofline derived
+            from the measured dense bf16 peak (TF32 runs at half the bf16
+            rate and 3xTF32 issues three TF32 products per output product);
+  cpu_baseline  the reference's own CPU code (oracle/_ref, built from the
+            reference sources) on the same workload, all host threads;
+  also      the large fp32 GEMM [8192x4096]@[4096x16384] (+bias via beta=1).
+
+--impl reference runs only the reference CPU arm on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "project-jcore_b200"))
+import npl_b200 as nb  # noqa: E402
+
+N_IMG, C_IN, HW_IN, C_OUT, KSZ = 32, 64, 56, 64, 3
+CONV_FLOPS = 2.0 * N_IMG * C_OUT * C_IN * HW_IN * HW_IN * KSZ * KSZ
+GEMM_M, GEMM_K, GEMM_N = 8192, 4096, 16384
+GEMM_FLOPS = 2.0 * GEMM_M * GEMM_K * GEMM_N
+WORKLOAD = ("npl_conv2d_bn_activation fp32 NCHW 3x3 s1 p1: N=32 C_in=64 56x56 C_out=64, "
+            "inference BN + ReLU")
+
+
+def conv_inputs(seed: int = 0):
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(0, 1, (N_IMG, C_IN, HW_IN, HW_IN)).astype(np.float32)
+    w = rng.normal(0, np.sqrt(2 / (9 * C_IN)), (C_OUT, C_IN, KSZ, KSZ)).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, C_OUT).astype(np.float32)
+    beta = rng.uniform(-0.1, 0.1, C_OUT).astype(np.float32)
+    mean = rng.normal(0, 0.1, C_OUT).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, C_OUT).astype(np.float32)
+    return x, w, gamma, beta, mean, var
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "200"], stdout=self.file,
+                stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, reasons, mx = [], set(), None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [v.strip() for v in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, r[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference CPU arm
+# ---------------------------------------------------------------------------
+def reference_cpu(steps: int, warmup: int):
+    """Times the reference's own CPU implementation of the step (its
+    npl_conv2d_bn_activation -- which runs the conv only -- followed by its
+    npl_batch_norm and npl_relu) with all host threads. Returns
+    (TFLOP/s, cores, sample, median seconds)."""
+    ref_lib = REPO / "oracle" / "_ref" / "libnpl_ref.so"
+    if not ref_lib.exists():
+        return None
+    sys.stdout.flush()
+    devnull = os.open(os.devnull, os.O_WRONLY)
+    saved = os.dup(1)
+    os.dup2(devnull, 1)  # the reference prints on init and on every activation call
+    try:
+        return _reference_cpu_timed(ref_lib, steps, warmup)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(devnull)
+        os.close(saved)
+
+
+def _reference_cpu_timed(ref_lib, steps, warmup):
+    lib = C.CDLL(str(ref_lib))
+    nb.bind(lib, nb.NPL_SIGNATURES)
+    cores = os.cpu_count() or 1
+    cfg = nb.NplConfig()
+    lib.npl_get_default_config(C.byref(cfg))
+    cfg.num_threads = cores
+    if lib.npl_init(C.byref(cfg)) != 0:
+        return None
+    x, w, gamma, beta, mean, var = conv_inputs(0)
+    conv = np.zeros((N_IMG, C_OUT, HW_IN, HW_IN), np.float32)
+    bnout = np.zeros_like(conv)
+    y = np.zeros_like(conv)
+    keep = [x, w, conv, bnout, y]
+    tx, tw, tc, tb, ty = (nb.tensor(lib, a.ctypes.data, a.shape) for a in keep)
+    p = nb.conv_params(KSZ, KSZ, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    bn = nb.NplBatchnormParams(mean.ctypes.data, var.ctypes.data, gamma.ctypes.data,
+                               beta.ctypes.data, 1e-5, 0, 0.1)
+    def step():
+        assert lib.npl_conv2d_bn_activation(C.byref(tx), C.byref(tw), None, C.byref(p),
+                                            C.byref(bn), nb.NPL_ACT_RELU, C.byref(tc),
+                                            None) == 0
+        assert lib.npl_batch_norm(C.byref(tc), C.byref(bn), C.byref(tb), None) == 0
+        assert lib.npl_relu(C.byref(tb), C.byref(ty), None) == 0
+
+    times = []
+    for _ in range(max(1, min(warmup, 2))):
+        step()
+    budget_end = time.perf_counter() + 30.0
+    for _ in range(max(1, steps)):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > budget_end:
+            break
+    med = statistics.median(times)
+    sample = (f"full workload (32 images), {len(times)} timed steps, median; reference "
+              f"npl_conv2d_bn_activation (conv only) + npl_batch_norm + npl_relu, "
+              f"num_threads={cores}, OpenBLAS {cores} threads")
+    return CONV_FLOPS / med / 1e12, cores, sample, med
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    lib = nb.load()
+    rc = lib.npl_init(None)
+    if rc != 0:
+        raise RuntimeError(f"npl_init failed: {rc}")
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    x, w, gamma, beta, mean, var = conv_inputs(0)
+    tx = torch.from_numpy(x).to(dev)
+    tw = torch.from_numpy(w).to(dev)
+    tg, tb, tm, tv = (torch.from_numpy(a).to(dev) for a in (gamma, beta, mean, var))
+    ty = torch.empty((N_IMG, C_OUT, HW_IN, HW_IN), device=dev)
+    g = nb.conv_geom(N_IMG, C_IN, HW_IN, HW_IN, C_OUT, KSZ, KSZ, 1, 1)
+    ws = lib.nplk_conv_workspace_size(C.byref(g))
+    work = torch.empty(ws // 4 + 64, device=dev)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)  # 256 MiB > 126 MB L2
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def prepare():
+        r = lib.nplk_conv2d_prepare(sptr, C.byref(g), p(tw), None, p(tm), p(tv), p(tg), p(tb),
+                                    1e-5, p(work), ws)
+        assert r == 0, r
+
+    def run():
+        r = lib.nplk_conv2d_run(sptr, C.byref(g), p(tx), nb.NPL_ACT_RELU, 0.0, p(ty), p(work),
+                                ws, None)
+        assert r == 0, r
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        prepare()
+        run()
+    torch.cuda.synchronize()
+    if lib.nplk_read_status(sptr) != 0:
+        raise RuntimeError("conv kernel reported a pipeline timeout")
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    lib.nplk_take_launch_count()
+    for i in range(args.steps):
+        flush.zero_()  # outside the timed events
+        ev[i][0].record(stream)
+        prepare()
+        ev[i][1].record(stream)
+        run()
+        ev[i][2].record(stream)
+    torch.cuda.synchronize()
+    launches = int(lib.nplk_take_launch_count())
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    if lib.nplk_read_status(sptr) != 0:
+        raise RuntimeError("conv kernel reported a pipeline timeout")
+    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
+    conv_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    stats = torch.tensor([sum(step_ms) / len(step_ms), statistics.mean(conv_ms)],
+                         device=dev, dtype=torch.float64)
+    tot_launch = torch.tensor([launches], device=dev, dtype=torch.int64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot_launch, op=dist.ReduceOp.SUM)
+    ms_per_step, conv_kernel_ms = stats.tolist()
+
+    # ---- e2e through the public C ABI with pinned host buffers ----
+    hx = torch.from_numpy(x).pin_memory()
+    hw_ = torch.from_numpy(w).pin_memory()
+    hy = torch.empty((N_IMG, C_OUT, HW_IN, HW_IN)).pin_memory()
+    hg, hb, hm, hv = (torch.from_numpy(a).pin_memory() for a in (gamma, beta, mean, var))
+    t_x = nb.tensor(lib, hx.data_ptr(), hx.shape)
+    t_w = nb.tensor(lib, hw_.data_ptr(), hw_.shape)
+    t_y = nb.tensor(lib, hy.data_ptr(), hy.shape)
+    cp = nb.conv_params(KSZ, KSZ, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    bnp = nb.NplBatchnormParams(hm.data_ptr(), hv.data_ptr(), hg.data_ptr(), hb.data_ptr(),
+                                1e-5, 0, 0.1)
+
+    def api_step():
+        r = lib.npl_conv2d_bn_activation(C.byref(t_x), C.byref(t_w), None, C.byref(cp),
+                                         C.byref(bnp), nb.NPL_ACT_RELU, C.byref(t_y), None)
+        assert r == 0, r
+
+    for _ in range(args.warmup):
+        api_step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        api_step()  # synchronous: copies in, kernels, copy out
+    e2e_s = torch.tensor([(time.perf_counter() - t0) / args.steps], device=dev,
+                         dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_step = float(e2e_s.item())
+    h2d = hx.numel() * 4 + hw_.numel() * 4 + 4 * C_OUT * 4
+    d2h = hy.numel() * 4
+
+    # ---- parity spot check of the timed output (device result vs host API result) ----
+    torch.cuda.synchronize()
+    same = torch.allclose(ty.cpu(), hy, rtol=0, atol=0)
+
+    result = None
+    if rank == 0:
+        hbm_peak, bf16_peak, peak_src = measured_peaks()
+        tf32x3_peak = bf16_peak / 2.0 / 3.0
+        achieved = (CONV_FLOPS / 1e12) / (conv_kernel_ms / 1e3)
+        traffic = None
+        tp = REPO / "profiles" / "conv_igemm_traffic.json"
+        if tp.exists():
+            traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
+        value = world * CONV_FLOPS / (ms_per_step / 1e3) / 1e12
+        result = {
+            "metric": "fused conv2d+BN+ReLU TFLOP/s (npl_conv2d_bn_activation, 3xTF32)",
+            "value": round(value, 3),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32 (3xTF32 tensor-core products, fp32 accumulate)",
+            "data": "synthetic (seeded: BASELINE distributions)",
+            "config": {
+                "workload": WORKLOAD,
+                "per_gpu_batch": N_IMG,
+                "global_batch": N_IMG * world,
+                "parallelism": f"dp{world} (batch-sharded, no collective)",
+                "l2": "flushed between steps (256 MiB write, outside the timed events)",
+                "step": "nplk_conv2d_prepare (weight split + BN constants) + nplk_conv2d_run",
+            },
+            "e2e": {
+                "value": round(world * CONV_FLOPS / e2e_step / 1e12, 3),
+                "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "npl_conv2d_bn_activation on pinned host tensors (library stages)",
+            },
+            "roofline": {
+                "bound": "tensor",
+                "achieved": round(achieved, 2),
+                "peak": round(tf32x3_peak, 1),
+                "unit": "TFLOP/s",
+                "frac": round(achieved / tf32x3_peak, 4),
+                "traffic": traffic,
+                "kernel": "conv_igemm_3xtf32_kernel<64>",
+                "kernel_ms": round(conv_kernel_ms, 5),
+                "peak_basis": f"{peak_src} bf16 {bf16_peak} TFLOP/s / 2 (TF32) / 3 (3xTF32)",
+            },
+            "gpu_launches": int(tot_launch.item()),
+            "output_matches_api_path": bool(same),
+        }
+        if clocks:
+            result["clocks"] = clocks
+    return lib, result
+
+
+def gemm_also(lib, args, local_rank):
+    """Large-GEMM figure on one GPU: C = A@B + C (C pre-filled with the bias row)."""
+    import torch
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(GEMM_M, GEMM_K, device=dev, generator=gen)
+    B = torch.randn(GEMM_K, GEMM_N, device=dev, generator=gen) / 64.0
+    bias = torch.randn(GEMM_N, device=dev, generator=gen) * 0.02
+    Cm = torch.empty(GEMM_M, GEMM_N, device=dev)
+    ws = lib.nplk_gemm_workspace_size(GEMM_M, GEMM_N, GEMM_K)
+    work = torch.empty(ws // 4 + 64, device=dev)
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        Cm.copy_(bias.expand(GEMM_M, GEMM_N))
+        r = lib.nplk_gemm(sptr, GEMM_M, GEMM_N, GEMM_K, 1.0, p(A), GEMM_K, p(B), GEMM_N, 1.0,
+                          p(Cm), GEMM_N, None, 0, 0.0, 0, p(work), ws, None)
+        assert r == 0, r
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 10))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    for e0, e1 in evs:
+        Cm.copy_(bias.expand(GEMM_M, GEMM_N))
+        e0.record(stream)
+        r = lib.nplk_gemm(sptr, GEMM_M, GEMM_N, GEMM_K, 1.0, p(A), GEMM_K, p(B), GEMM_N, 1.0,
+                          p(Cm), GEMM_N, None, 0, 0.0, 0, p(work), ws, None)
+        assert r == 0, r
+        e1.record(stream)
+    torch.cuda.synchronize()
+    if lib.nplk_read_status(sptr) != 0:
+        raise RuntimeError("GEMM kernel reported a pipeline timeout")
+    ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    # spot parity on a few rows against fp64
+    rows = torch.arange(0, GEMM_M, GEMM_M // 8, device=dev)
+    ref = A[rows].double() @ B.double() + bias.double()
+    err = ((Cm[rows].double() - ref).abs().max() / ref.abs().max()).item()
+    del A, B, Cm, work
+    torch.cuda.empty_cache()
+    return {"workload": "npl_matmul fp32 [8192x4096]@[4096x16384] + bias (beta=1), 1 GPU",
+            "value": round(GEMM_FLOPS / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4), "normwise_err_sampled_rows": err,
+            "step": "split A and B^T into tf32 hi/lo + tcgen05 GEMM"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-gemm", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        r = reference_cpu(args.steps, args.warmup)
+        if r is None:
+            print(json.dumps({"impl": "reference",
+                              "unavailable": "oracle/_ref/libnpl_ref.so was not built"}))
+            return
+        tflops, cores, sample, med = r
+        print(json.dumps({
+            "impl": "reference",
+            "metric": "fused conv2d+BN+ReLU TFLOP/s (npl_conv2d_bn_activation, 3xTF32)",
+            "value": round(tflops, 5), "unit": "TFLOP/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic (seeded: BASELINE distributions)",
+            "config": {"workload": WORKLOAD, "per_gpu_batch": N_IMG,
+                       "global_batch": N_IMG, "parallelism": "host CPU (reference build)"},
+            "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOP/s", "cores": cores,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": round(tflops, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        lib, result = run_b200(args, rank, world, local_rank)
+        if rank == 0:
+            if world == 1 and not args.no_gemm:
+                result["also"] = {"gemm": gemm_also(lib, args, local_rank)}
+            if world == 1:
+                r = reference_cpu(3, 1)
+                if r is not None:
+                    tflops, cores, sample, _ = r
+                    result["cpu_baseline"] = {"value": round(tflops, 5), "unit": "TFLOP/s",
+                                              "cores": cores, "kind": "reference",
+                                              "sample": sample}
+            print(json.dumps(result))
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -91,6 +91,19 @@ NPL_API int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const flo
                       float act_alpha, float *out, void *workspace, size_t workspace_bytes,
                       int *status);
 
+/* The two halves of nplk_conv2d_fused, for callers that reuse one set of
+ * weights across many inputs (inference): prepare writes the tap-major tf32
+ * hi/lo split of w and the per-channel epilogue constants (bias, BN) into the
+ * workspace; run executes the implicit-GEMM kernel against a prepared
+ * workspace. Without BN parameters the constants are the identity. */
+NPL_API int nplk_conv2d_prepare(void *stream, const nplk_conv_geom_t *g, const float *w,
+                                const float *bias, const float *bn_mean, const float *bn_var,
+                                const float *bn_gamma, const float *bn_beta, float bn_eps,
+                                void *workspace, size_t workspace_bytes);
+NPL_API int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x, int act,
+                            float act_alpha, float *out, const void *workspace,
+                            size_t workspace_bytes, int *status);
+
 /* ---- bandwidth-bound primitives -------------------------------------------- */
 
 /* Depthwise conv, weights [C,1,kh,kw]; g->c_out must equal g->c_in. Dilation

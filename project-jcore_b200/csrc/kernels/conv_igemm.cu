@@ -62,7 +62,7 @@ struct ConvParams {
   int K, k_blocks, m_blocks, n_blocks;
   const float *ep;
   int cout_pad;
-  int has_bn, act;
+  int act;
   float act_alpha;
   int *status;
 };
@@ -274,7 +274,8 @@ __global__ void __launch_bounds__(kConvThreads, 1)
             const int co = co0 + j;
             if (co < p.Cout) {
               float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + ep_bias[co];
-              if (p.has_bn) t = ep_gamma[co] * (t - ep_mean[co]) * ep_inv[co] + ep_beta[co];
+              // Without BN the constants are gamma 1, mean 0, inv_std 1, beta 0.
+              t = ep_gamma[co] * (t - ep_mean[co]) * ep_inv[co] + ep_beta[co];
               yb[static_cast<int64_t>(co) * p.HoWo] = apply_act(t, p.act, p.act_alpha);
             }
           }
@@ -399,39 +400,59 @@ extern "C" size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g) {
   return c.w_bytes + c.ep_bytes;
 }
 
-extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,
-                                 const float *w, const float *bias, const float *bn_mean,
-                                 const float *bn_var, const float *bn_gamma,
-                                 const float *bn_beta, float bn_eps, int act, float act_alpha,
-                                 float *out, void *workspace, size_t workspace_bytes,
-                                 int *status) {
+namespace {
+
+// Checks geometry and workspace shared by prepare and run.
+int check_conv_call(const nplk_conv_geom_t *g, void *workspace, size_t workspace_bytes,
+                    ConvPlan *c) {
   int rc = validate_conv_geom(g);
   if (rc) return rc;
-  if (!x || !w || !out) return kErrInvalidArg;
-  const ConvPlan c = plan_conv(g);
-  if (!workspace || workspace_bytes < c.w_bytes + c.ep_bytes ||
+  *c = plan_conv(g);
+  if (!workspace || workspace_bytes < c->w_bytes + c->ep_bytes ||
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return kErrInvalidArg;
-  if (!status) status = device_status_word();
-  if (!status) return kErrInternal;
+  return kOk;
+}
+
+}  // namespace
+
+extern "C" int nplk_conv2d_prepare(void *stream, const nplk_conv_geom_t *g, const float *w,
+                                   const float *bias, const float *bn_mean,
+                                   const float *bn_var, const float *bn_gamma,
+                                   const float *bn_beta, float bn_eps, void *workspace,
+                                   size_t workspace_bytes) {
+  ConvPlan c;
+  int rc = check_conv_call(g, workspace, workspace_bytes, &c);
+  if (rc) return rc;
+  if (!w) return kErrInvalidArg;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float *wsplit = static_cast<float *>(workspace);
   float *ep = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + c.w_bytes);
-
   const int64_t wsplit_elems = c.cout_pad * 2 * c.kp;
-  {
-    const int threads = 256;
-    int64_t blocks = ceil_div(wsplit_elems / 2, threads);
-    if (blocks > 4096) blocks = 4096;
-    conv_prep_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(
-        w, static_cast<int>(g->c_out), static_cast<int>(g->c_in), static_cast<int>(g->kh),
-        static_cast<int>(g->kw), static_cast<int>(c.kp), c.bnc, wsplit, wsplit_elems, bias,
-        bn_mean, bn_var, bn_gamma, bn_beta, bn_eps, ep, static_cast<int>(c.cout_pad));
-    count_launch();
-    rc = launch_result();
-    if (rc) return rc;
-  }
+  const int threads = 256;
+  int64_t blocks = ceil_div(wsplit_elems / 2, threads);
+  if (blocks > 4096) blocks = 4096;
+  conv_prep_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(
+      w, static_cast<int>(g->c_out), static_cast<int>(g->c_in), static_cast<int>(g->kh),
+      static_cast<int>(g->kw), static_cast<int>(c.kp), c.bnc, wsplit, wsplit_elems, bias,
+      bn_mean, bn_var, bn_gamma, bn_beta, bn_eps, ep, static_cast<int>(c.cout_pad));
+  count_launch();
+  return launch_result();
+}
 
+extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
+                               int act, float act_alpha, float *out, const void *workspace,
+                               size_t workspace_bytes, int *status) {
+  ConvPlan c;
+  int rc = check_conv_call(g, const_cast<void *>(workspace), workspace_bytes, &c);
+  if (rc) return rc;
+  if (!x || !out) return kErrInvalidArg;
+  if (!status) status = device_status_word();
+  if (!status) return kErrInternal;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float *wsplit = static_cast<const float *>(workspace);
+  const float *ep =
+      reinterpret_cast<const float *>(static_cast<const uint8_t *>(workspace) + c.w_bytes);
   ConvParams prm{};
   prm.x = x;
   prm.y = out;
@@ -459,10 +480,22 @@ extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const 
   prm.n_blocks = static_cast<int>(c.n_blocks);
   prm.ep = ep;
   prm.cout_pad = static_cast<int>(c.cout_pad);
-  prm.has_bn = bn_mean != nullptr ? 1 : 0;
   prm.act = act;
   prm.act_alpha = act_alpha;
   prm.status = status;
   if (c.bnc == 64) return launch_conv<64>(s, c, wsplit, prm);
   return launch_conv<128>(s, c, wsplit, prm);
+}
+
+extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                 const float *w, const float *bias, const float *bn_mean,
+                                 const float *bn_var, const float *bn_gamma,
+                                 const float *bn_beta, float bn_eps, int act, float act_alpha,
+                                 float *out, void *workspace, size_t workspace_bytes,
+                                 int *status) {
+  if (!x || !w || !out) return kErrInvalidArg;
+  int rc = nplk_conv2d_prepare(stream, g, w, bias, bn_mean, bn_var, bn_gamma, bn_beta, bn_eps,
+                               workspace, workspace_bytes);
+  if (rc) return rc;
+  return nplk_conv2d_run(stream, g, x, act, act_alpha, out, workspace, workspace_bytes, status);
 }

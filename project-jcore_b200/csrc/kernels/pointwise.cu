@@ -28,7 +28,7 @@ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 // inv_std = 1/sqrt(var+eps) (npl_activation_norm.cpp:389-398). Each block
 // first computes the per-channel constants into shared memory.
 // ---------------------------------------------------------------------------
-constexpr int kBnMaxSmemChannels = 4096;
+constexpr int kBnMaxSmemChannels = 3072;  // 48 KB of float4: the default smem limit
 
 template <bool kVec>
 __global__ void bn_infer_kernel(const float *__restrict__ x, float *__restrict__ y,

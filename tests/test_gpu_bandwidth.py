@@ -1,0 +1,241 @@
+"""Parity of the bandwidth-bound NPL primitives (depthwise conv, batch norm,
+activations, global average pool, softmax, layer norm, pooling, add/mul) with
+the oracle: full-size BASELINE shapes plus ragged and edge cases. Integer-like
+work (max pooling, ReLU, depthwise with the reference's FMA order) is checked
+bit for bit; reductions and transcendentals within 1e-5 normwise."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import support as S
+from support import nb
+
+pytestmark = pytest.mark.gpu
+
+
+def run(lib, name, *args):
+    rc = S.npl_call(lib, name, *args)
+    assert rc == 0, (name, lib.npl_strerror(rc))
+
+
+def test_bandwidth_chain_config4_full():
+    # depthwise 3x3 pad 1 -> BN -> ReLU -> GAP -> softmax over 512 channels,
+    # N=256, C=512, 14x14, inputs N(0,1), dw weights N(0,0.3).
+    lib = S.gpu_lib()
+    rng = S.rng(0)
+    x = rng.normal(0, 1, (256, 512, 14, 14)).astype(np.float32)
+    w = rng.normal(0, 0.3, (512, 1, 3, 3)).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, 512).astype(np.float32)
+    beta = rng.uniform(-0.1, 0.1, 512).astype(np.float32)
+    mean = rng.normal(0, 0.1, 512).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, 512).astype(np.float32)
+    h = S.HostTensors(lib)
+    dw = np.zeros_like(x)
+    p = nb.conv_params(3, 3, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    run(lib, "npl_depthwise_conv2d", h.t(x), h.t(w), None, p, h.t(dw), None)
+    r_dw = S.o_depthwise(x, w, pad=(1, 1))
+    assert S.normwise_err(dw, r_dw) < 1e-6
+    bnp = nb.NplBatchnormParams(mean.ctypes.data, var.ctypes.data, gamma.ctypes.data,
+                                beta.ctypes.data, 1e-5, 0, 0.1)
+    bn = np.zeros_like(x)
+    run(lib, "npl_batch_norm", h.t(r_dw), bnp, h.t(bn), None)
+    r_bn = S.o_batch_norm(r_dw, mean, var, gamma, beta)
+    assert S.normwise_err(bn, r_bn) < 1e-6
+    relu = np.zeros_like(x)
+    run(lib, "npl_relu", h.t(r_bn), h.t(relu), None)
+    r_relu = S.o_activation(r_bn, 1)
+    assert np.array_equal(relu.view(np.uint32), r_relu.view(np.uint32))
+    gap = np.zeros((256, 512), np.float32)
+    run(lib, "npl_global_avg_pool", h.t(r_relu), h.t(gap), None)
+    r_gap = S.o_gap(r_relu)
+    assert S.normwise_err(gap, r_gap) < 1e-6
+    sm = np.zeros_like(gap)
+    run(lib, "npl_softmax", h.t(r_gap), 1, h.t(sm), None)
+    assert S.normwise_err(sm, S.o_softmax(r_gap, 1)) < 1e-5
+
+
+def test_depthwise_golden_and_edges():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "depthwise.npz"))
+    h = S.HostTensors(lib)
+    y = np.zeros_like(g["y"])
+    p = nb.conv_params(3, 3, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    run(lib, "npl_depthwise_conv2d", h.t(g["x"]), h.t(g["w"]), h.t(g["bias"]), p, h.t(y), None)
+    assert S.normwise_err(y, g["y"]) < 1e-6
+    rng = S.rng(2)
+    x = rng.normal(0, 1, (3, 5, 11, 9)).astype(np.float32)
+    w = rng.normal(0, 0.3, (5, 1, 5, 3)).astype(np.float32)
+    p = nb.conv_params(5, 3, (2, 1), (2, 0), padding=nb.NPL_PAD_EXPLICIT)
+    ref = S.o_depthwise(x, w, (2, 1), (2, 0))
+    y = np.zeros_like(ref)
+    run(lib, "npl_depthwise_conv2d", h.t(x), h.t(w), None, p, h.t(y), None)
+    assert S.normwise_err(y, ref) < 1e-6
+
+
+def test_batch_norm_golden_inference_and_training():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "batch_norm.npz"))
+    h = S.HostTensors(lib)
+    y = np.zeros_like(g["x"])
+    bnp = nb.NplBatchnormParams(g["mean"].ctypes.data, g["var"].ctypes.data,
+                                g["gamma"].ctypes.data, g["beta"].ctypes.data, 1e-5, 0, 0.1)
+    run(lib, "npl_batch_norm", h.t(g["x"]), bnp, h.t(y), None)
+    assert S.normwise_err(y, g["y"]) < 1e-6
+    rm, rv = g["mean"].copy(), g["var"].copy()
+    bnt = nb.NplBatchnormParams(rm.ctypes.data, rv.ctypes.data, g["gamma"].ctypes.data,
+                                g["beta"].ctypes.data, 1e-5, 1, 0.1)
+    yt = np.zeros_like(g["x"])
+    run(lib, "npl_batch_norm", h.t(g["x"]), bnt, h.t(yt), None)
+    assert S.normwise_err(yt, g["y_train"]) < 1e-5
+    assert S.normwise_err(rm, g["run_mean"]) < 1e-5
+    assert S.normwise_err(rv, g["run_var"]) < 1e-5
+    # missing statistics and wrong rank are rejected like the reference
+    bad = nb.NplBatchnormParams(None, g["var"].ctypes.data, None, None, 1e-5, 0, 0.1)
+    assert S.npl_call(lib, "npl_batch_norm", h.t(g["x"]), bad, h.t(y), None) == \
+        nb.NPL_ERR_INVALID_ARG
+    x2 = np.zeros((4, 5), np.float32)
+    assert S.npl_call(lib, "npl_batch_norm", h.t(x2), bnp, h.t(x2.copy()), None) == \
+        nb.NPL_ERR_SHAPE_MISMATCH
+
+
+ACTS = {"relu": 1, "relu6": 2, "tanh": 3, "sigmoid": 4, "gelu": 5, "swish": 6, "leaky": 7,
+        "elu": 8, "selu": 9, "softplus": 10}
+
+
+@pytest.mark.parametrize("name", sorted(ACTS))
+def test_activation_golden(name):
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "activations.npz"))
+    h = S.HostTensors(lib)
+    y = np.zeros_like(g["x"])
+    run(lib, "npl_activation", h.t(g["x"]), ACTS[name], h.t(y), None)
+    if name in ("relu", "relu6", "leaky"):
+        assert np.array_equal(y.view(np.uint32), g[name].view(np.uint32))
+    else:
+        assert S.normwise_err(y, g[name]) < 1e-5
+
+
+def test_relu_inplace_ragged_and_leaky():
+    lib = S.gpu_lib()
+    rng = S.rng(3)
+    base = rng.normal(0, 1, 10007).astype(np.float32)
+    x = base[1:].copy()  # odd length
+    h = S.HostTensors(lib)
+    t = h.t(x)
+    run(lib, "npl_relu", t, t, None)  # in place
+    assert np.array_equal(x, np.where(base[1:] < 0, 0, base[1:]).astype(np.float32))
+    y = np.zeros_like(base)
+    run(lib, "npl_leaky_relu", h.t(base), C.c_float(0.2), h.t(y), None)
+    assert np.array_equal(y, S.o_activation(base, 7, 0.2))
+
+
+def test_softmax_axes():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "softmax.npz"))
+    h = S.HostTensors(lib)
+    y2 = np.zeros_like(g["x2"])
+    run(lib, "npl_softmax", h.t(g["x2"]), 1, h.t(y2), None)
+    assert S.normwise_err(y2, g["y2"]) < 1e-5
+    y3 = np.zeros_like(g["x3"])
+    run(lib, "npl_softmax", h.t(g["x3"]), -2, h.t(y3), None)
+    assert S.normwise_err(y3, g["y3"]) < 1e-5
+    rng = S.rng(4)
+    for shape, axis in [((3, 1000), 1), ((7, 2048), -1), ((2, 3, 33), 2), ((5, 6), 0)]:
+        x = rng.normal(0, 4, shape).astype(np.float32)
+        y = np.zeros_like(x)
+        run(lib, "npl_softmax", h.t(x), axis, h.t(y), None)
+        assert S.normwise_err(y, S.o_softmax(x, axis)) < 1e-5
+    assert S.npl_call(lib, "npl_softmax", h.t(g["x2"]), 2, h.t(y2), None) == \
+        nb.NPL_ERR_INVALID_ARG
+
+
+def test_layer_norm_golden_and_config5_rows():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "layer_norm.npz"))
+    h = S.HostTensors(lib)
+    y = np.zeros_like(g["x"])
+    run(lib, "npl_layer_norm", h.t(g["x"]), nb.NplLayernormParams(None, None, 1e-5, 128),
+        h.t(y), None)
+    assert S.normwise_err(y, g["y"]) < 1e-5
+    y2 = np.zeros_like(g["x2"])
+    p2 = nb.NplLayernormParams(g["gamma2"].ctypes.data, g["beta2"].ctypes.data, 1e-5, 7)
+    run(lib, "npl_layer_norm", h.t(g["x2"]), p2, h.t(y2), None)
+    assert S.normwise_err(y2, g["y2"]) < 1e-5
+    # the large-GEMM case normalises rows of 16384 (gamma=1, beta=0)
+    rng = S.rng(5)
+    x = np.maximum(rng.normal(0, 2, (64, 16384)), 0).astype(np.float32)
+    y = np.zeros_like(x)
+    run(lib, "npl_layer_norm", h.t(x), nb.NplLayernormParams(None, None, 1e-5, 16384),
+        h.t(y), None)
+    assert S.normwise_err(y, S.o_layer_norm(x, 16384)) < 1e-5
+    for cols in (3, 1000, 40000):  # generic path and row lengths beyond registers
+        x = rng.normal(0, 1, (5, cols)).astype(np.float32)
+        y = np.zeros_like(x)
+        run(lib, "npl_layer_norm", h.t(x), nb.NplLayernormParams(None, None, 1e-5, cols),
+            h.t(y), None)
+        assert S.normwise_err(y, S.o_layer_norm(x, cols)) < 1e-5
+
+
+def test_pooling_golden_and_stem_size():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "pooling.npz"))
+    h = S.HostTensors(lib)
+    for key, kind, cip in (("ymax", nb.NPL_POOL_MAX, 0), ("yavg", nb.NPL_POOL_AVG, 0),
+                           ("yavg_pad", nb.NPL_POOL_AVG, 1)):
+        y = np.zeros_like(g[key])
+        run(lib, "npl_pooling", h.t(g["x"]), nb.NplPoolingParams(3, 3, 2, 2, 1, 1, kind, cip),
+            h.t(y), None)
+        if kind == nb.NPL_POOL_MAX:
+            assert np.array_equal(y, g[key])
+        else:
+            assert S.normwise_err(y, g[key]) < 1e-6
+    yg = np.zeros_like(g["yg"])
+    run(lib, "npl_global_avg_pool", h.t(g["xg"]), h.t(yg), None)
+    assert S.normwise_err(yg, g["yg"]) < 1e-6
+    # stem max pool at full size: [128,64,112,112] -> [128,64,56,56]
+    rng = S.rng(6)
+    x = rng.normal(0, 1, (128, 64, 112, 112)).astype(np.float32)
+    y = np.zeros((128, 64, 56, 56), np.float32)
+    run(lib, "npl_pooling", h.t(x), nb.NplPoolingParams(3, 3, 2, 2, 1, 1, nb.NPL_POOL_MAX, 0),
+        h.t(y), None)
+    assert np.array_equal(y, S.o_pool(x, (3, 3), (2, 2), (1, 1), 0))
+    # exact output shape is required (npl_pooling.cpp:121-124)
+    bad = np.zeros((128, 64, 55, 56), np.float32)
+    assert S.npl_call(lib, "npl_pooling", h.t(x),
+                      nb.NplPoolingParams(3, 3, 2, 2, 1, 1, nb.NPL_POOL_MAX, 0), h.t(bad),
+                      None) == nb.NPL_ERR_SHAPE_MISMATCH
+
+
+def test_gap_known_answer_and_output_forms():
+    lib = S.gpu_lib()
+    h = S.HostTensors(lib)
+    x = np.ones((2, 64, 7, 7), np.float32)
+    y4 = np.zeros((2, 64, 1, 1), np.float32)
+    run(lib, "npl_global_avg_pool", h.t(x), h.t(y4), None)
+    assert np.all(np.abs(y4 - 1) < 1e-3)  # npl_test.cpp:520-555
+    rng = S.rng(7)
+    x = rng.normal(0, 1, (3, 5, 9, 7)).astype(np.float32)  # hw = 63, not a multiple of 4
+    y2 = np.zeros((3, 5), np.float32)
+    run(lib, "npl_global_avg_pool", h.t(x), h.t(y2), None)
+    assert S.normwise_err(y2, S.o_gap(x)) < 1e-6
+
+
+def test_add_mul_variants():
+    lib = S.gpu_lib()
+    g = dict(np.load(S.GOLDEN / "elementwise.npz"))
+    h = S.HostTensors(lib)
+    out = np.zeros_like(g["a"])
+    run(lib, "npl_add", h.t(g["a"]), h.t(g["b"]), h.t(out), None)
+    assert np.array_equal(out, g["add"])
+    run(lib, "npl_mul", h.t(g["a"]), h.t(g["b"]), h.t(out), None)
+    assert np.array_equal(out, g["mul"])
+    out4 = np.zeros_like(g["x4"])
+    run(lib, "npl_mul", h.t(g["x4"]), h.t(g["s4"]), h.t(out4), None)
+    assert np.array_equal(out4, g["mulc"])
+    s = np.array([3.0], np.float32)
+    run(lib, "npl_mul", h.t(g["a"]), h.t(s), h.t(out), None)
+    assert np.array_equal(out, g["a"] * 3.0)
+    # broadcasting add is unsupported, as in the reference (:453-467)
+    assert S.npl_call(lib, "npl_add", h.t(g["a"]), h.t(s), h.t(out), None) == \
+        nb.NPL_ERR_UNSUPPORTED
