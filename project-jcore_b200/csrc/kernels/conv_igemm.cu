@@ -3,7 +3,10 @@
 //
 // GEMM view: D[m][co] = sum_k A[m][k] * W'[co][k]
 //   m  = (n, oh, ow)           output pixel, M = N*Ho*Wo
-//   k  = (kh, kw, ci)          tap-major reduction index, K = KH*KW*Cin
+//   k  = (ci, kh, kw) in one of two orders, K = KH*KW*Cin:
+//        Cin % 32 == 0: channel-block-major, k = ((cb*KH*KW) + tap)*32 + ci%32,
+//                       so each 32-wide k-block is one tap over 32 channels;
+//        otherwise:     tap-major, k = tap*Cin + ci
 //   A[m][k] = x[n][ci][oh*sh - pt + kh*dh][ow*sw - pl + kw*dw]  (0 outside)
 //   W'[co][k] = w[co][ci][kh][kw]
 // Reference semantics: ExecuteConvDirect (advanced/neural_layer/src/
@@ -13,18 +16,20 @@
 // activation, i.e. what npl_conv2d_bn_activation is specified to compute
 // (the reference itself stops after the conv, npl_convolution.cpp:116-126).
 //
-// No im2col matrix is materialised. Per persistent CTA (416 threads):
-//   warps 0-7   gather A: each thread owns one pixel row and 16 of the 32
+// No im2col matrix is materialised. Per persistent CTA:
+//   producer warps, in groups of two (one group per shared-memory stage),
+//               gather A: each thread owns two pixel rows and the 32
 //               k-columns of a stage, loads them straight from NCHW global
 //               memory (coalesced along ow), splits each value into tf32
 //               hi/lo and writes both into 128-byte-swizzled shared memory;
-//               thread 0 also TMA-loads the matching [W'_hi; W'_lo] slab;
-//   warp 8      issues tcgen05.mma: MMA(A_hi, [W_hi; W_lo]) with N = 2*BNC and
+//               the group's first thread also TMA-loads the matching
+//               [W'_hi; W'_lo] slab;
+//   MMA warp    issues tcgen05.mma: MMA(A_hi, [W_hi; W_lo]) with N = 2*BNC and
 //               MMA(A_lo, W_hi) with N = BNC into a TMEM accumulator;
-//   warps 9-12  epilogue: out = act(BN(D[:, :BNC] + D[:, BNC:] + bias)),
-//               one coalesced HBM write per output element.
-// The weights are prepared by conv_prep_kernel (permute to tap-major, split,
-// zero-pad) together with the per-channel epilogue constants.
+//   4 epilogue warps: out = act(BN(D[:, :BNC] + D[:, BNC:] + bias)), one
+//               coalesced HBM write per output element.
+// The weights are prepared by conv_prep_kernel (permute to the k order,
+// split, zero-pad) together with the per-channel epilogue constants.
 #include <cuda_runtime.h>
 
 #include "nplk_device.cuh"
@@ -35,18 +40,25 @@ namespace nplk {
 
 constexpr int kConvBM = 128;
 constexpr int kConvBK = 32;
-constexpr int kConvProducerWarps = 8;
-constexpr int kConvMmaWarp = kConvProducerWarps;  // warps after it: epilogue
-constexpr int kConvThreads = (kConvProducerWarps + 1 + 4) * 32;
+
+// Producer warps work in groups of two; group g fills shared-memory stage g
+// for every work item (tile, k-block) whose index is g modulo the number of
+// stages, so as many stages are being gathered concurrently as there are
+// stages, each with 64 independent loads per thread in flight.
+constexpr int kConvGroupWarps = 2;
 
 template <int BNC>
 struct ConvTraits {
   static constexpr int kStages = BNC == 64 ? 4 : 3;
+  static constexpr int kProducerWarps = kStages * kConvGroupWarps;
+  static constexpr int kMmaWarp = kProducerWarps;  // warps after it: epilogue
+  static constexpr int kThreads = (kProducerWarps + 1 + 4) * 32;
   static constexpr int kAStageBytes = 2 * kConvBM * kConvBK * 4;  // hi + lo: 32 KB
   static constexpr int kBStageBytes = 2 * BNC * kConvBK * 4;
   static constexpr int kAccCols = 2 * BNC;
   static constexpr int kTmemCols = 2 * kAccCols;
-  static constexpr int kSmemBytes = 1024 + kStages * (kAStageBytes + kBStageBytes) + 256;
+  static constexpr int kSmemBytes =
+      1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20;  // + epilogue constants
 };
 
 // Per-channel epilogue constants, [5][cout_pad]: bias, mean, gamma, beta,
@@ -67,8 +79,25 @@ struct ConvParams {
   int *status;
 };
 
-template <int BNC>
-__global__ void __launch_bounds__(kConvThreads, 1)
+// Epilogue activation selected at compile time for the common cases.
+enum { kEpiActNone = 0, kEpiActRelu = 1, kEpiActAny = 2 };
+
+template <int kAct>
+__device__ __forceinline__ float epilogue_act(float t, int act, float alpha) {
+  if (kAct == kEpiActNone) return t;
+  if (kAct == kEpiActRelu) return t < 0.0f ? 0.0f : t;  // std::max(t, 0)
+  return apply_act(t, act, alpha);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// kFastC: C is a multiple of 32, so every 32-wide k-block is one filter tap
+// across 32 consecutive channels (k ordered channel-block-major, see
+// conv_prep_kernel) and the gather needs no per-element tap bookkeeping.
+template <int BNC, bool kFastC, int kAct>
+__global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
   using T = ConvTraits<BNC>;
   extern __shared__ uint8_t smem_raw[];
@@ -82,13 +111,15 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   uint64_t *acc_empty = acc_full + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  float4 *ep_s = reinterpret_cast<float4 *>(smem_b + T::kStages * T::kBStageBytes + 256);
+  float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < T::kStages; ++s) {
-      mbar_init(&full[s], kConvProducerWarps + 1);
+      mbar_init(&full[s], kConvGroupWarps + 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -99,7 +130,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&map_w);
   }
-  if (warp == kConvMmaWarp) {
+  if (warp == T::kMmaWarp) {
     tmem_alloc(tmem_slot, T::kTmemCols);
     tmem_relinquish();
   }
@@ -109,91 +140,137 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = p.m_blocks * p.n_blocks;
 
-  if (warp < kConvProducerWarps) {
-    // ---------------- A gather + weight TMA ----------------
-    const int row = threadIdx.x & (kConvBM - 1);
-    const int half = threadIdx.x >> 7;  // which 16 of the 32 k-columns
-    int stage = 0;
+  if (warp < T::kProducerWarps) {
+    // ---------------- A gather + weight TMA (group = stage) ----------------
+    const int group = warp / kConvGroupWarps;
+    const int gt = threadIdx.x - group * kConvGroupWarps * 32;  // 0..63 within the group
+    const int stage = group;
     uint32_t phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mb = tile / p.n_blocks;
-      const int nb = tile - mb * p.n_blocks;
-      const int m = mb * kConvBM + row;
-      const bool valid = m < p.M;
-      int n = 0, oh = 0, ow = 0;
-      if (valid) {
-        n = m / static_cast<int>(p.HoWo);
-        const int pix = m - n * static_cast<int>(p.HoWo);
-        oh = pix / p.Wo;
-        ow = pix - oh * p.Wo;
-      }
-      const int ih0 = oh * p.sh - p.pt;
-      const int iw0 = ow * p.sw - p.pl;
-      const float *xb = p.x + static_cast<int64_t>(n) * p.CHW;
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
-                       kStatusTimeoutProducer))
-          goto producer_done;
-        if (threadIdx.x == 0) {
-          mbar_arrive_expect_tx(&full[stage], T::kBStageBytes);
-          tma_load_2d(&map_w, &full[stage], smem_b + stage * T::kBStageBytes, kb * kConvBK,
-                      nb * 2 * BNC);
+    const int my_tiles = num_tiles > static_cast<int>(blockIdx.x)
+                             ? (num_tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                             : 0;
+    const int items = my_tiles * p.k_blocks;
+    int cur_tile = -1;
+    int ih0[2] = {0, 0}, iw0[2] = {0, 0};
+    bool valid[2] = {false, false};
+    const float *xb[2] = {p.x, p.x};
+    int nb = 0;
+    for (int it = group; it < items; it += T::kStages) {
+      const int lt = it / p.k_blocks;
+      const int kb = it - lt * p.k_blocks;
+      const int tile = blockIdx.x + lt * gridDim.x;
+      if (tile != cur_tile) {
+        cur_tile = tile;
+        const int mb = tile / p.n_blocks;
+        nb = tile - mb * p.n_blocks;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int m = mb * kConvBM + gt + 64 * r;
+          valid[r] = m < p.M;
+          int n = 0, oh = 0, ow = 0;
+          if (valid[r]) {
+            n = m / static_cast<int>(p.HoWo);
+            const int pix = m - n * static_cast<int>(p.HoWo);
+            oh = pix / p.Wo;
+            ow = pix - oh * p.Wo;
+          }
+          ih0[r] = oh * p.sh - p.pt;
+          iw0[r] = ow * p.sw - p.pl;
+          xb[r] = p.x + static_cast<int64_t>(n) * p.CHW;
         }
-        // Decode the first of this thread's 16 k indices, then walk them.
-        int k = kb * kConvBK + half * 16;
+      }
+      // Gather 2 rows x 32 k into registers before waiting for the stage.
+      float v[2][32];
+      if (kFastC) {
+        const int taps = p.KH * p.KW;
+        const int cb = kb / taps;
+        const int tap = kb - cb * taps;
+        const int kh = tap / p.KW;
+        const int kw = tap - kh * p.KW;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int ih = ih0[r] + kh * p.dh, iw = iw0[r] + kw * p.dw;
+          const bool ok = valid[r] && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                          static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+          const float *base =
+              xb[r] + static_cast<int64_t>(cb * kConvBK) * p.HW + static_cast<int64_t>(ih) * p.W + iw;
+          if (ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[r][j] = __ldg(base + static_cast<int64_t>(j) * p.HW);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[r][j] = 0.0f;
+          }
+        }
+      } else {
+        int k = kb * kConvBK;
         int tap = k / p.C;
         int ci = k - tap * p.C;
         int kh = tap / p.KW;
         int kw = tap - kh * p.KW;
-        int ih = ih0 + kh * p.dh;
-        int iw = iw0 + kw * p.dw;
-        bool ok = valid && kh < p.KH && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
-                  static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
-        const float *ptr = xb + static_cast<int64_t>(ci) * p.HW +
-                           static_cast<int64_t>(ih) * p.W + iw;
-        float v[16];
+        bool ok[2];
+        const float *ptr[2];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          v[j] = ok ? __ldg(ptr) : 0.0f;
-          ptr += p.HW;
+        for (int r = 0; r < 2; ++r) {
+          const int ih = ih0[r] + kh * p.dh, iw = iw0[r] + kw * p.dw;
+          ok[r] = valid[r] && kh < p.KH &&
+                  static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                  static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+          ptr[r] = xb[r] + static_cast<int64_t>(ci) * p.HW + static_cast<int64_t>(ih) * p.W + iw;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          v[0][j] = ok[0] ? __ldg(ptr[0]) : 0.0f;
+          v[1][j] = ok[1] ? __ldg(ptr[1]) : 0.0f;
+          ptr[0] += p.HW;
+          ptr[1] += p.HW;
           if (++ci == p.C) {
             ci = 0;
             if (++kw == p.KW) {
               kw = 0;
               ++kh;
             }
-            ih = ih0 + kh * p.dh;
-            iw = iw0 + kw * p.dw;
-            ok = valid && kh < p.KH &&
-                 static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
-                 static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
-            ptr = xb + static_cast<int64_t>(ih) * p.W + iw;
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int ih = ih0[r] + kh * p.dh, iw = iw0[r] + kw * p.dw;
+              ok[r] = valid[r] && kh < p.KH &&
+                      static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                      static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+              ptr[r] = xb[r] + static_cast<int64_t>(ih) * p.W + iw;
+            }
           }
         }
-        uint8_t *a_hi = smem_a + stage * T::kAStageBytes;
-        uint8_t *a_lo = a_hi + kConvBM * 128;
+      }
+      if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+        break;
+      if (gt == 0) {
+        mbar_arrive_expect_tx(&full[stage], T::kBStageBytes);
+        tma_load_2d(&map_w, &full[stage], smem_b + stage * T::kBStageBytes, kb * kConvBK,
+                    nb * 2 * BNC);
+      }
+      uint8_t *a_hi = smem_a + stage * T::kAStageBytes;
+      uint8_t *a_lo = a_hi + kConvBM * 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+      for (int r = 0; r < 2; ++r) {
+        const int row = gt + 64 * r;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
           float4 hi, lo;
-          tf32_split(v[4 * c + 0], hi.x, lo.x);
-          tf32_split(v[4 * c + 1], hi.y, lo.y);
-          tf32_split(v[4 * c + 2], hi.z, lo.z);
-          tf32_split(v[4 * c + 3], hi.w, lo.w);
-          const uint32_t off = sw128_offset(row, half * 4 + c);
+          tf32_split_trunc(v[r][4 * c + 0], hi.x, lo.x);
+          tf32_split_trunc(v[r][4 * c + 1], hi.y, lo.y);
+          tf32_split_trunc(v[r][4 * c + 2], hi.z, lo.z);
+          tf32_split_trunc(v[r][4 * c + 3], hi.w, lo.w);
+          const uint32_t off = sw128_offset(row, c);
           *reinterpret_cast<float4 *>(a_hi + off) = hi;
           *reinterpret_cast<float4 *>(a_lo + off) = lo;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[stage]);
-        if (++stage == T::kStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[stage]);
+      phase ^= 1u;
     }
-  producer_done:;
-  } else if (warp == kConvMmaWarp) {
+  } else if (warp == T::kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc_2n = umma_idesc_tf32(kConvBM, 2 * BNC);
@@ -234,23 +311,32 @@ __global__ void __launch_bounds__(kConvThreads, 1)
     mma_done:;
     }
   } else {
-    // ---------------- epilogue (warps 9..12) ----------------
+    // ---------------- epilogue (4 warps, one per TMEM lane quadrant) ----------------
+    // The tile's per-channel constants are staged in shared memory (all lanes
+    // read the same channel, so each read is a broadcast).
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const float *ep_bias = p.ep + kEpBias * p.cout_pad;
-    const float *ep_mean = p.ep + kEpMean * p.cout_pad;
-    const float *ep_gamma = p.ep + kEpGamma * p.cout_pad;
-    const float *ep_beta = p.ep + kEpBeta * p.cout_pad;
-    const float *ep_inv = p.ep + kEpInvStd * p.cout_pad;
+    const int et = threadIdx.x - (T::kMmaWarp + 1) * 32;  // 0..127
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
-        break;
-      tc_fence_after_sync();
       const int mb = tile / p.n_blocks;
       const int nb = tile - mb * p.n_blocks;
+      mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
+      // All four warps pass this barrier before anyone rewrites the constants
+      // of the previous tile, and they leave together if the CTA aborted.
+      named_barrier_sync(1, 128);
+      if (*abort_flag) break;
+      for (int i = et; i < BNC; i += 128) {
+        const int co = nb * BNC + i;
+        ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
+                              p.ep[kEpGamma * p.cout_pad + co],
+                              p.ep[kEpInvStd * p.cout_pad + co]);
+        ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
+      }
+      named_barrier_sync(1, 128);
+      tc_fence_after_sync();
       const int m = mb * kConvBM + row;
       const bool valid = m < p.M;
       int n = 0, pix = 0;
@@ -269,14 +355,23 @@ __global__ void __launch_bounds__(kConvThreads, 1)
         tmem_wait_ld2(v, w);
         const int co0 = nb * BNC + c0;
         if (valid) {
+          if (co0 + 32 <= p.Cout) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int co = co0 + j;
-            if (co < p.Cout) {
-              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + ep_bias[co];
-              // Without BN the constants are gamma 1, mean 0, inv_std 1, beta 0.
-              t = ep_gamma[co] * (t - ep_mean[co]) * ep_inv[co] + ep_beta[co];
-              yb[static_cast<int64_t>(co) * p.HoWo] = apply_act(t, p.act, p.act_alpha);
+            for (int j = 0; j < 32; ++j) {
+              const float4 q = ep_s[c0 + j];
+              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
+              // Without BN the constants are mean 0, gamma 1, inv_std 1, beta 0.
+              t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
+              yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (co0 + j >= p.Cout) continue;
+              const float4 q = ep_s[c0 + j];
+              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
+              t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
+              yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
             }
           }
         }
@@ -288,7 +383,7 @@ __global__ void __launch_bounds__(kConvThreads, 1)
   }
 
   __syncthreads();
-  if (warp == kConvMmaWarp) {
+  if (warp == T::kMmaWarp) {
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, T::kTmemCols);
   }
@@ -312,8 +407,18 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
     const int co = static_cast<int>(rowg);
     float x = 0.0f;
     if (co < Cout && k < K) {
-      const int tap = k / C;
-      const int ci = k - tap * C;
+      int ci, tap;
+      if (C % kConvBK == 0) {
+        // channel-block-major: k = ((cb * KH*KW) + tap) * 32 + ci_in
+        const int kb = k / kConvBK;
+        const int cb = kb / (KH * KW);
+        tap = kb - cb * (KH * KW);
+        ci = cb * kConvBK + (k - kb * kConvBK);
+      } else {
+        // tap-major: k = tap * C + ci
+        tap = k / C;
+        ci = k - tap * C;
+      }
       const int kh = tap / KW;
       const int kw = tap - kh * KW;
       x = w[((static_cast<int64_t>(co) * C + ci) * KH + kh) * KW + kw];
@@ -356,21 +461,37 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g) {
   return c;
 }
 
-template <int BNC>
+template <int BNC, bool kFastC, int kAct>
 int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
   using T = ConvTraits<BNC>;
   CUtensorMap map_w;
   int rc = encode_tmap_2d_f32_sw128(&map_w, wsplit, c.kp, c.n_blocks * 2 * BNC, c.kp * 4,
                                     kConvBK, 2 * BNC);
   if (rc) return rc;
-  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC>),
-                           T::kSmemBytes);
+  rc = ensure_dynamic_smem(
+      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kFastC, kAct>), T::kSmemBytes);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_igemm_3xtf32_kernel<BNC><<<grid, kConvThreads, T::kSmemBytes, s>>>(map_w, prm);
+  conv_igemm_3xtf32_kernel<BNC, kFastC, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm);
   count_launch();
   return launch_result();
+}
+
+template <int BNC, bool kFastC>
+int dispatch_act(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
+  if (prm.act == 0) return launch_conv<BNC, kFastC, kEpiActNone>(s, c, wsplit, prm);
+  if (prm.act == 1) return launch_conv<BNC, kFastC, kEpiActRelu>(s, c, wsplit, prm);
+  return launch_conv<BNC, kFastC, kEpiActAny>(s, c, wsplit, prm);
+}
+
+int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm,
+                  bool fast) {
+  if (c.bnc == 64)
+    return fast ? dispatch_act<64, true>(s, c, wsplit, prm)
+                : dispatch_act<64, false>(s, c, wsplit, prm);
+  return fast ? dispatch_act<128, true>(s, c, wsplit, prm)
+              : dispatch_act<128, false>(s, c, wsplit, prm);
 }
 
 }  // namespace
@@ -483,8 +604,7 @@ extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const fl
   prm.act = act;
   prm.act_alpha = act_alpha;
   prm.status = status;
-  if (c.bnc == 64) return launch_conv<64>(s, c, wsplit, prm);
-  return launch_conv<128>(s, c, wsplit, prm);
+  return dispatch_conv(s, c, wsplit, prm, g->c_in % kConvBK == 0);
 }
 
 extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,

@@ -162,13 +162,21 @@ def test_layer_norm_golden_and_config5_rows():
     p2 = nb.NplLayernormParams(g["gamma2"].ctypes.data, g["beta2"].ctypes.data, 1e-5, 7)
     run(lib, "npl_layer_norm", h.t(g["x2"]), p2, h.t(y2), None)
     assert S.normwise_err(y2, g["y2"]) < 1e-5
-    # the large-GEMM case normalises rows of 16384 (gamma=1, beta=0)
+    # The large-GEMM case normalises rows of 16384 (gamma=1, beta=0). The
+    # reference sums each row serially in fp32, which is itself ~4e-5 away from
+    # the exact result on such rows; the kernel's tree reduction is checked
+    # against an fp64 layer norm tightly and against the oracle at the parity
+    # tolerance.
     rng = S.rng(5)
     x = np.maximum(rng.normal(0, 2, (64, 16384)), 0).astype(np.float32)
     y = np.zeros_like(x)
     run(lib, "npl_layer_norm", h.t(x), nb.NplLayernormParams(None, None, 1e-5, 16384),
         h.t(y), None)
-    assert S.normwise_err(y, S.o_layer_norm(x, 16384)) < 1e-5
+    x64 = x.astype(np.float64)
+    m = x64.mean(axis=1, keepdims=True)
+    exact = (x64 - m) / np.sqrt(((x64 - m) ** 2).mean(axis=1, keepdims=True) + 1e-5)
+    assert S.normwise_err(y, exact) < 1e-5
+    assert S.normwise_err(y, S.o_layer_norm(x, 16384)) < 1e-4
     for cols in (3, 1000, 40000):  # generic path and row lengths beyond registers
         x = rng.normal(0, 1, (5, cols)).astype(np.float32)
         y = np.zeros_like(x)
