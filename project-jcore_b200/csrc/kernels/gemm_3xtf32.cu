@@ -144,6 +144,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_2n = umma_idesc_tf32(kGemmBM, 2 * BN);
       const uint32_t idesc_n = umma_idesc_tf32(kGemmBM, BN);
+      const uint64_t a_desc0 = umma_desc_sw128(smem_u32(smem_a));
+      const uint64_t b_desc0 = umma_desc_sw128(smem_u32(smem_b));
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -159,19 +161,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma))
             goto mma_done;
           tc_fence_after_sync();
-          const uint32_t a_addr = smem_u32(smem_a + stage * T::kAStageBytes);
-          const uint32_t b_addr = smem_u32(smem_b + stage * T::kBStageBytes);
+          // Descriptors of the stage; a 32-byte step along K adds 2 to the
+          // start-address field (address >> 4).
+          const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage * (T::kAStageBytes >> 4));
+          const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage * (T::kBStageBytes >> 4));
+          constexpr uint64_t kLoOff = (kGemmBM * 128) >> 4;
+          if (p.one_pass) {
 #pragma unroll
-          for (int kk = 0; kk < kGemmBK / 8; ++kk) {
-            const uint64_t a_hi = umma_desc_sw128(a_addr + kk * 32);
-            const uint64_t a_lo = umma_desc_sw128(a_addr + kGemmBM * 128 + kk * 32);
-            const uint64_t b = umma_desc_sw128(b_addr + kk * 32);
-            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
-            if (p.one_pass) {
-              mma_tf32_ss(d_tmem, a_hi, b, idesc_n, accum);
-            } else {
-              mma_tf32_ss(d_tmem, a_hi, b, idesc_2n, accum);
-              mma_tf32_ss(d_tmem, a_lo, b, idesc_n, 1u);
+            for (int kk = 0; kk < kGemmBK / 8; ++kk)
+              mma_tf32_ss(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc_n,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kGemmBK / 8; ++kk) {
+              mma_tf32_ss(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc_2n,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ss(d_tmem, a_desc + kLoOff + 2 * kk, b_desc + 2 * kk, idesc_n, 1u);
             }
           }
           mma_commit(&empty[stage]);
