@@ -104,6 +104,23 @@ NPL_API int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float
                             float act_alpha, float *out, const void *workspace,
                             size_t workspace_bytes, int *status);
 
+/* nplk_conv2d_fused for callers that cannot allocate device memory (hosts
+ * that reserve their whole device budget up front, code running inside an
+ * allocator callback, foreign-language callers that must not trigger the
+ * device-wide synchronisation cudaMalloc/cudaFree can cause). No counterpart
+ * in the reference: it has no device memory at all. The weight split and
+ * epilogue constants live in an 8 MiB array inside the library that every
+ * GPU loading the library keeps until exit; larger geometries are rejected
+ * with NPL_ERR_UNSUPPORTED. The first call on a device looks up that array's
+ * address, so it should precede any stream capture. All calls on a device
+ * share the array: calls that overlap on the GPU race. status may be NULL
+ * (an internal word is used and cleared by each call). Allocates nothing. */
+NPL_API int nplk_conv2d_fused_noalloc(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                      const float *w, const float *bias, const float *bn_mean,
+                                      const float *bn_var, const float *bn_gamma,
+                                      const float *bn_beta, float bn_eps, int act,
+                                      float act_alpha, float *out, int *status);
+
 /* ---- bandwidth-bound primitives -------------------------------------------- */
 
 /* Depthwise conv, weights [C,1,kh,kw]; g->c_out must equal g->c_in. Dilation

@@ -165,6 +165,8 @@ NPLK_SIGNATURES = {
     "nplk_conv2d_prepare": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP,
                                       C.c_size_t]),
     "nplk_conv2d_run": (C.c_int, [_VP, _G, _VP, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
+    "nplk_conv2d_fused_noalloc": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
+                                            C.c_int, _F, _VP, _VP]),
     "nplk_depthwise_conv2d": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP]),
     "nplk_batch_norm_infer": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _F]),
     "nplk_batch_norm_stats": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP]),
