@@ -412,6 +412,66 @@ def gemm_also(lib, args, local_rank):
             "step": "split A and B^T into tf32 hi/lo + tcgen05 GEMM"}
 
 
+def gemm_dist(args, rank, world, local_rank):
+    """Column-sharded large GEMM on `world` GPUs: each rank computes its block
+    of C = A @ B + bias (A replicated), the blocks are all-gathered over NCCL
+    and relaid to row-major C. Device time per step (max over ranks) is
+    reported for the GEMM alone and for GEMM + all-gather + relayout."""
+    import torch
+    import torch.distributed as dist
+    from npl_b200 import dist as nd
+
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    A = torch.randn(GEMM_M, GEMM_K, device=dev, generator=gen)
+    B = torch.randn(GEMM_K, GEMM_N, device=dev, generator=gen) / 64.0
+    bias = torch.randn(GEMM_N, device=dev, generator=gen) * 0.02
+    lib = nb.load()
+    w = GEMM_N // world
+    ws = lib.nplk_gemm_workspace_size(GEMM_M, w, GEMM_K)
+    work = torch.empty(ws // 4 + 64, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        local = nd.column_sharded_gemm(A, B, bias, world, rank, workspace=work, gather=False)
+        e_mid.record(stream)
+        return nd.gather_column_blocks(local, world)
+
+    for _ in range(2):
+        e_mid = torch.cuda.Event(enable_timing=True)
+        step()
+    torch.cuda.synchronize()
+    n = max(3, min(args.steps, 10))
+    g_ms, t_ms = [], []
+    dist.barrier()
+    for _ in range(n):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e_mid = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        full = step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        g_ms.append(e0.elapsed_time(e_mid))
+        t_ms.append(e0.elapsed_time(e1))
+    dist.barrier()
+    if lib.nplk_read_status(C.c_void_p(stream.cuda_stream)) != 0:
+        raise RuntimeError("GEMM kernel reported a pipeline timeout")
+    t = torch.tensor([statistics.mean(g_ms), statistics.mean(t_ms)], device=dev,
+                     dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rows = torch.arange(0, GEMM_M, GEMM_M // 4, device=dev)
+    ref = A[rows].double() @ B.double() + bias.double()
+    err = ((full[rows].double() - ref).abs().max() / ref.abs().max()).item()
+    gm, tm = t.tolist()
+    return {"workload": f"npl_matmul fp32 [8192x4096]@[4096x16384] + bias, B/C column-sharded "
+                        f"over {world} GPUs, NCCL all-gather of C + relayout",
+            "gemm_only_value": round(GEMM_FLOPS / (gm / 1e3) / 1e12, 2),
+            "end_to_end_value": round(GEMM_FLOPS / (tm / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "gemm_ms": round(gm, 4), "gemm_allgather_relayout_ms": round(tm, 4),
+            "normwise_err_sampled_rows": err}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,6 +519,10 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         lib, result = run_b200(args, rank, world, local_rank)
+        if world > 1 and not args.no_gemm:
+            gd = gemm_dist(args, rank, world, local_rank)
+            if rank == 0:
+                result["also"] = {"gemm_column_sharded": gd}
         if rank == 0:
             if world == 1 and not args.no_gemm:
                 result["also"] = {"gemm": gemm_also(lib, args, local_rank)}

@@ -1,0 +1,108 @@
+"""Small, fixed workloads for profiling the NPL kernels (for example under
+``ncu``). Each case allocates its inputs on cuda:0, runs the kernel a few times
+and checks the kernel status word.
+
+    python -m npl_b200.profile_cases conv      # 3x3 conv+BN+ReLU, N=32 64->64 56x56
+    python -m npl_b200.profile_cases stem      # 7x7/s2 conv+BN+ReLU, N=16 3->64 224x224
+    python -m npl_b200.profile_cases gemm      # 4096x4096x8192 3xTF32 GEMM
+    python -m npl_b200.profile_cases chain     # depthwise, BN, ReLU, GAP, softmax 256x512x14x14
+    python -m npl_b200.profile_cases layernorm # 8192 x 16384 rows
+
+Run from the package directory (``project-jcore_b200``) or with it on sys.path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import sys
+
+
+def _setup():
+    import torch
+    from . import load
+    torch.cuda.set_device(0)
+    lib = load()
+    return torch, lib, C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def case_conv(reps: int = 3, n: int = 32, c: int = 64, hw: int = 56, cout: int = 64,
+              k: int = 3, stride: int = 1, pad: int = 1):
+    from . import conv_geom
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.rand(n, c, hw, hw, device="cuda", generator=gen)
+    w = torch.randn(cout, c, k, k, device="cuda", generator=gen) * 0.05
+    bn = [torch.rand(cout, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    g = conv_geom(n, c, hw, hw, cout, k, k, stride, pad)
+    y = torch.empty(n, cout, g.h_out, g.w_out, device="cuda")
+    ws = lib.nplk_conv_workspace_size(C.byref(g))
+    work = torch.empty(ws // 4 + 64, device="cuda")
+    for _ in range(reps):
+        rc = lib.nplk_conv2d_fused(s, C.byref(g), _p(x), _p(w), None, _p(bn[0]), _p(bn[1]),
+                                   _p(bn[2]), _p(bn[3]), 1e-5, 1, 0.0, _p(y), _p(work), ws, None)
+        assert rc == 0, rc
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+
+
+def case_stem(reps: int = 3):
+    case_conv(reps, n=16, c=3, hw=224, cout=64, k=7, stride=2, pad=3)
+
+
+def case_gemm(reps: int = 3, m: int = 4096, n: int = 4096, k: int = 8192):
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(m, k, device="cuda", generator=gen)
+    b = torch.randn(k, n, device="cuda", generator=gen) / 64.0
+    c = torch.empty(m, n, device="cuda")
+    ws = lib.nplk_gemm_workspace_size(m, n, k)
+    work = torch.empty(ws // 4 + 64, device="cuda")
+    for _ in range(reps):
+        rc = lib.nplk_gemm(s, m, n, k, 1.0, _p(a), k, _p(b), n, 0.0, _p(c), n, None, 0, 0.0, 0,
+                           _p(work), ws, None)
+        assert rc == 0, rc
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+
+
+def case_chain(reps: int = 3):
+    from . import conv_geom
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    n, c, hw = 256, 512, 14
+    x = torch.randn(n, c, hw, hw, device="cuda", generator=gen)
+    w = torch.randn(c, 1, 3, 3, device="cuda", generator=gen) * 0.3
+    bn = [torch.rand(c, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    t1, t2 = torch.empty_like(x), torch.empty_like(x)
+    gap = torch.empty(n, c, device="cuda")
+    sm = torch.empty_like(gap)
+    g = conv_geom(n, c, hw, hw, c, 3, 3, 1, 1)
+    for _ in range(reps):
+        assert lib.nplk_depthwise_conv2d(s, C.byref(g), _p(x), _p(w), None, _p(t1)) == 0
+        assert lib.nplk_batch_norm_infer(s, n, c, hw * hw, _p(t1), _p(t2), _p(bn[0]), _p(bn[1]),
+                                         _p(bn[2]), _p(bn[3]), 1e-5) == 0
+        assert lib.nplk_activation(s, t2.numel(), _p(t2), _p(t2), 1, 0.0, 0) == 0
+        assert lib.nplk_global_avg_pool(s, n * c, hw * hw, _p(t2), _p(gap)) == 0
+        assert lib.nplk_softmax(s, n, c, 1, _p(gap), _p(sm)) == 0
+    torch.cuda.synchronize()
+
+
+def case_layernorm(reps: int = 3):
+    torch, lib, s = _setup()
+    x = torch.randn(8192, 16384, device="cuda")
+    y = torch.empty_like(x)
+    for _ in range(reps):
+        assert lib.nplk_layer_norm(s, 8192, 16384, _p(x), _p(y), None, None, 1e-5) == 0
+    torch.cuda.synchronize()
+
+
+CASES = {"conv": case_conv, "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
+         "layernorm": case_layernorm}
+
+if __name__ == "__main__":
+    name = sys.argv[1] if len(sys.argv) > 1 else "conv"
+    CASES[name]()
+    print("ok", name)
