@@ -73,9 +73,17 @@ typedef struct {
   int64_t h_out, w_out;
 } nplk_conv_geom_t;
 
-/* Scratch bytes for nplk_conv2d_fused with this geometry (split weights and
- * per-channel epilogue constants). */
+/* Scratch bytes for nplk_conv2d_fused with this geometry: split weights,
+ * per-channel epilogue constants and, when c_in is a multiple of 32 and the
+ * geometry suits the TMA im2col mode, two NHWC copies of the input (tf32 hi
+ * and lo parts) that the fastest kernel reads. */
 NPL_API size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g);
+
+/* Smallest workspace the conv entry points accept (split weights and
+ * epilogue constants only). With less than nplk_conv_workspace_size bytes
+ * the conv runs on the direct-gather kernel, which reads NCHW x itself; the
+ * results are the same bit for bit. */
+NPL_API size_t nplk_conv_workspace_min_size(const nplk_conv_geom_t *g);
 
 /* out = act(BN(conv(x, w) + bias)) as one implicit-GEMM kernel: no im2col is
  * materialised, BN (inference form gamma*(t-mean)/sqrt(var+eps)+beta, the
@@ -95,14 +103,29 @@ NPL_API int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const flo
  * weights across many inputs (inference): prepare writes the tap-major tf32
  * hi/lo split of w and the per-channel epilogue constants (bias, BN) into the
  * workspace; run executes the implicit-GEMM kernel against a prepared
- * workspace. Without BN parameters the constants are the identity. */
+ * workspace (and, given the full workspace size, first rewrites x into the
+ * NHWC planes after the prepared part). Without BN parameters the constants
+ * are the identity. */
 NPL_API int nplk_conv2d_prepare(void *stream, const nplk_conv_geom_t *g, const float *w,
                                 const float *bias, const float *bn_mean, const float *bn_var,
                                 const float *bn_gamma, const float *bn_beta, float bn_eps,
                                 void *workspace, size_t workspace_bytes);
 NPL_API int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x, int act,
-                            float act_alpha, float *out, const void *workspace,
+                            float act_alpha, float *out, void *workspace,
                             size_t workspace_bytes, int *status);
+
+/* nplk_conv2d_run in two steps, for the TMA-im2col path only (geometries
+ * where nplk_conv_workspace_size exceeds nplk_conv_workspace_min_size, with
+ * the full workspace): stage_input rewrites x as the NHWC tf32 hi/lo planes
+ * in the workspace, run_staged runs the conv kernel on them. One staged input
+ * serves any number of run_staged calls of the same geometry (for example
+ * two convolutions of one input). Both return NPL_ERR_UNSUPPORTED where the
+ * path does not apply. */
+NPL_API int nplk_conv2d_stage_input(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                    void *workspace, size_t workspace_bytes);
+NPL_API int nplk_conv2d_run_staged(void *stream, const nplk_conv_geom_t *g, int act,
+                                   float act_alpha, float *out, void *workspace,
+                                   size_t workspace_bytes, int *status);
 
 /* nplk_conv2d_fused for callers that cannot allocate device memory (hosts
  * that reserve their whole device budget up front, code running inside an

@@ -1,0 +1,153 @@
+// Pieces shared by the fused conv kernels (direct NCHW gather in
+// conv_igemm.cu, TMA im2col over NHWC split planes in conv_im2col.cu, shared
+// TMA windows over a raw NHWC plane in conv_window.cu): the
+// GEMM tile shape, kernel parameters, per-channel epilogue constants and the
+// accumulator-drain epilogue.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "nplk_device.cuh"
+#include "ptx_sm100.cuh"
+
+namespace nplk {
+
+constexpr int kConvBM = 128;  // output pixels per tile (TMEM lanes)
+constexpr int kConvBK = 32;   // k per stage (one 128-byte swizzle row of fp32)
+
+// Per-channel epilogue constants, [5][cout_pad]: bias, mean, gamma, beta,
+// 1/sqrt(var+eps).
+enum { kEpBias = 0, kEpMean = 1, kEpGamma = 2, kEpBeta = 3, kEpInvStd = 4, kEpCount = 5 };
+
+struct ConvParams {
+  const float *x;
+  float *y;
+  int C, H, W, Cout, KH, KW, sh, sw, pt, pl, dh, dw, Ho, Wo;
+  int64_t HW, HoWo, CHW;
+  int M;
+  // GEMM rows: "virtual" output pixels (n, oh, ow') with ow' < Wv, Mv of them.
+  // Wv = Wo except for the window kernel, whose traversal also visits the
+  // (KW-1)*dw columns right of each output row (computed, never stored).
+  int Wv, Mv;
+  int K, k_blocks, m_blocks, n_blocks;
+  const float *ep;
+  int cout_pad;
+  int act;
+  float act_alpha;
+  int *status;
+};
+
+// Epilogue activation selected at compile time for the common cases.
+enum { kEpiActNone = 0, kEpiActRelu = 1, kEpiActAny = 2 };
+
+template <int kAct>
+__device__ __forceinline__ float epilogue_act(float t, int act, float alpha) {
+  if (kAct == kEpiActNone) return t;
+  if (kAct == kEpiActRelu) return t < 0.0f ? 0.0f : t;  // std::max(t, 0)
+  return apply_act(t, act, alpha);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Drains one finished accumulator tile (GEMM rows mb*128.., channels
+// nb*BNC..) to NCHW, skipping rows that are not output pixels:
+// out = act(gamma*((D[:, :BNC] + D[:, BNC:] + bias) - mean)*inv_std + beta).
+// Called by the 4 epilogue warps (warp quad = TMEM lane quadrant, et = 0..127
+// across them); `acc_tmem` is the accumulator's first column. The tile's
+// constants are staged in shared memory (every lane reads the same channel,
+// so each read is a broadcast). Returns false when the CTA aborted.
+template <int BNC, int kAct>
+__device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t acc_tmem,
+                                                   int quad, int lane, int et, int mb, int nb,
+                                                   float4 *ep_s, float *ep_beta_s,
+                                                   uint64_t *acc_full, uint32_t acc_phase,
+                                                   volatile int *abort_flag) {
+  mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
+  // All four warps pass this barrier before anyone rewrites the constants of
+  // the previous tile, and they leave together if the CTA aborted.
+  named_barrier_sync(1, 128);
+  if (*abort_flag) return false;
+  for (int i = et; i < BNC; i += 128) {
+    const int co = nb * BNC + i;
+    ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
+                          p.ep[kEpGamma * p.cout_pad + co], p.ep[kEpInvStd * p.cout_pad + co]);
+    ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
+  }
+  named_barrier_sync(1, 128);
+  tc_fence_after_sync();
+  const int m = mb * kConvBM + quad * 32 + lane;  // GEMM row (virtual pixel)
+  bool valid = m < p.Mv;
+  int n = 0, pix = 0;
+  if (valid) {
+    const int howv = p.Ho * p.Wv;
+    n = m / howv;
+    const int rem = m - n * howv;
+    const int oh = rem / p.Wv;
+    const int ow = rem - oh * p.Wv;
+    valid = ow < p.Wo;
+    pix = oh * p.Wo + ow;
+  }
+  float *yb = p.y + static_cast<int64_t>(n) * p.Cout * p.HoWo + pix;
+  const uint32_t t_row = acc_tmem + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BNC; c0 += 32) {
+    uint32_t v[32], w[32];
+    tmem_ld32(t_row + c0, v);
+    tmem_ld32(t_row + BNC + c0, w);
+    tmem_wait_ld2(v, w);
+    const int co0 = nb * BNC + c0;
+    if (valid) {
+      if (co0 + 32 <= p.Cout) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float4 q = ep_s[c0 + j];
+          float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
+          // Without BN the constants are mean 0, gamma 1, inv_std 1, beta 0.
+          t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
+          yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (co0 + j >= p.Cout) continue;
+          const float4 q = ep_s[c0 + j];
+          float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
+          t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
+          yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
+        }
+      }
+    }
+  }
+  return true;
+}
+
+// Launches the TMA-im2col conv (conv_im2col.cu) for channel counts that are a
+// multiple of 32: x_hi / x_lo are the input's NHWC tf32 hi/lo planes written
+// by launch_nchw_to_nhwc_split. Returns an NPL error code.
+int launch_conv_im2col(cudaStream_t s, int bnc, const float *wsplit, int64_t kp,
+                       int64_t n_blocks, const float *x_hi, const float *x_lo,
+                       const ConvParams &prm, int n_img);
+
+// True when launch_conv_im2col supports the geometry (corner and traversal
+// ranges of the im2col tensor map, plane size).
+bool conv_im2col_supported(const ConvParams &prm, int n_img);
+
+// x[n][c][hw] -> hi[n][hw][c], lo[n][hw][c] with hi = tf32 truncation of x
+// and lo = x - hi (exact); with lo == nullptr, hi[n][hw][c] = x (no split).
+// c must be a multiple of 32.
+int launch_nchw_to_nhwc_split(cudaStream_t s, const float *x, float *hi, float *lo, int n,
+                              int c, int64_t hw);
+
+// Window conv (conv_window.cu) over the raw NHWC plane x_nhwc; its GEMM rows
+// are the virtual pixels given by conv_window_rows.
+int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
+                       const float *x_nhwc, ConvParams prm, int n_img);
+bool conv_window_supported(const ConvParams &prm, int n_img);
+void conv_window_rows(const ConvParams &p, int *wv, int64_t *mv);
+
+}  // namespace nplk

@@ -34,14 +34,10 @@
 
 #include <cstdlib>
 
-#include "nplk_device.cuh"
+#include "conv_common.cuh"
 #include "nplk_host.h"
-#include "ptx_sm100.cuh"
 
 namespace nplk {
-
-constexpr int kConvBM = 128;
-constexpr int kConvBK = 32;
 
 // Producer warps work in groups of two; group g fills shared-memory stage g
 // for every work item (tile, k-block) whose index is g modulo the number of
@@ -62,38 +58,6 @@ struct ConvTraits {
   static constexpr int kSmemBytes =
       1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20;  // + epilogue constants
 };
-
-// Per-channel epilogue constants, [5][cout_pad]: bias, mean, gamma, beta,
-// 1/sqrt(var+eps).
-enum { kEpBias = 0, kEpMean = 1, kEpGamma = 2, kEpBeta = 3, kEpInvStd = 4, kEpCount = 5 };
-
-struct ConvParams {
-  const float *x;
-  float *y;
-  int C, H, W, Cout, KH, KW, sh, sw, pt, pl, dh, dw, Ho, Wo;
-  int64_t HW, HoWo, CHW;
-  int M;
-  int K, k_blocks, m_blocks, n_blocks;
-  const float *ep;
-  int cout_pad;
-  int act;
-  float act_alpha;
-  int *status;
-};
-
-// Epilogue activation selected at compile time for the common cases.
-enum { kEpiActNone = 0, kEpiActRelu = 1, kEpiActAny = 2 };
-
-template <int kAct>
-__device__ __forceinline__ float epilogue_act(float t, int act, float alpha) {
-  if (kAct == kEpiActNone) return t;
-  if (kAct == kEpiActRelu) return t < 0.0f ? 0.0f : t;  // std::max(t, 0)
-  return apply_act(t, act, alpha);
-}
-
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 // kFastC: C is a multiple of 32, so every 32-wide k-block is one filter tap
 // across 32 consecutive channels (k ordered channel-block-major, see
@@ -157,6 +121,8 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     bool valid[2] = {false, false};
     const float *xb[2] = {p.x, p.x};
     int nb = 0;
+    bool issued = false;  // a weight copy was issued into this group's stage
+    uint32_t issued_phase = 0;
     for (int it = group; it < items; it += T::kStages) {
       const int lt = it / p.k_blocks;
       const int kb = it - lt * p.k_blocks;
@@ -249,6 +215,8 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
         mbar_arrive_expect_tx(&full[stage], T::kBStageBytes);
         tma_load_2d(&map_w, &full[stage], smem_b + stage * T::kBStageBytes, kb * kConvBK,
                     nb * 2 * BNC);
+        issued = true;
+        issued_phase = phase;
       }
       uint8_t *a_hi = smem_a + stage * T::kAStageBytes;
       uint8_t *a_lo = a_hi + kConvBM * 128;
@@ -272,6 +240,9 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
       if (lane == 0) mbar_arrive(&full[stage]);
       phase ^= 1u;
     }
+    // Let the last weight copy land before the CTA can exit (it already has
+    // unless the CTA aborted).
+    if (gt == 0 && issued) mbar_drain(&full[stage], issued_phase);
   } else if (warp == T::kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -315,10 +286,7 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     }
   } else {
     // ---------------- epilogue (4 warps, one per TMEM lane quadrant) ----------------
-    // The tile's per-channel constants are staged in shared memory (all lanes
-    // read the same channel, so each read is a broadcast).
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;
     const int et = threadIdx.x - (T::kMmaWarp + 1) * 32;  // 0..127
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -326,386 +294,9 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       const int mb = tile / p.n_blocks;
       const int nb = tile - mb * p.n_blocks;
-      mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
-      // All four warps pass this barrier before anyone rewrites the constants
-      // of the previous tile, and they leave together if the CTA aborted.
-      named_barrier_sync(1, 128);
-      if (*abort_flag) break;
-      for (int i = et; i < BNC; i += 128) {
-        const int co = nb * BNC + i;
-        ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
-                              p.ep[kEpGamma * p.cout_pad + co],
-                              p.ep[kEpInvStd * p.cout_pad + co]);
-        ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
-      }
-      named_barrier_sync(1, 128);
-      tc_fence_after_sync();
-      const int m = mb * kConvBM + row;
-      const bool valid = m < p.M;
-      int n = 0, pix = 0;
-      if (valid) {
-        n = m / static_cast<int>(p.HoWo);
-        pix = m - n * static_cast<int>(p.HoWo);
-      }
-      float *yb = p.y + static_cast<int64_t>(n) * p.Cout * p.HoWo + pix;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * T::kAccCols);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BNC; c0 += 32) {
-        uint32_t v[32], w[32];
-        tmem_ld32(t_row + c0, v);
-        tmem_ld32(t_row + BNC + c0, w);
-        tmem_wait_ld2(v, w);
-        const int co0 = nb * BNC + c0;
-        if (valid) {
-          if (co0 + 32 <= p.Cout) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float4 q = ep_s[c0 + j];
-              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
-              // Without BN the constants are mean 0, gamma 1, inv_std 1, beta 0.
-              t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
-              yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (co0 + j >= p.Cout) continue;
-              const float4 q = ep_s[c0 + j];
-              float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
-              t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
-              yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
-            }
-          }
-        }
-      }
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-    }
-  }
-
-  __syncthreads();
-  if (warp == T::kMmaWarp) {
-    tc_fence_after_sync();
-    tmem_dealloc(tmem_base, T::kTmemCols);
-  }
-}
-
-// Variant for output-channel blocks of 64 that stages the A operand in tensor
-// memory instead of shared memory: each producer warp owns one TMEM lane
-// quadrant (32 pixel rows), gathers its rows' 32 k values, splits them and
-// writes hi/lo with tcgen05.st; the MMA then reads A from TMEM. Shared memory
-// only holds the weight stages, which leaves most of the SM's L1 to the
-// gather. TMEM columns: [0,256) two accumulators of 2*64, [256,512) four A
-// stages of 64 (hi 32 + lo 32).
-#ifndef NPL_CONV_TMEM_A_STAGES
-#define NPL_CONV_TMEM_A_STAGES 3
-#endif
-constexpr int kConvTmemAStages = NPL_CONV_TMEM_A_STAGES;
-
-template <int S>
-struct ConvTmemATraits {
-  static constexpr int BNC = 64;
-  static constexpr int kStages = S;       // A stages in TMEM (one producer group each)
-  static constexpr int kBStages = 8;      // weight stages in shared memory
-  static constexpr int kGroupWarps = 4;   // one warp per TMEM lane quadrant
-  static constexpr int kProducerWarps = kStages * kGroupWarps;
-  static constexpr int kTmaWarp = kProducerWarps;
-  static constexpr int kMmaWarp = kProducerWarps + 1;
-  static constexpr int kThreads = (kProducerWarps + 2 + 4) * 32;
-  static constexpr int kBStageBytes = 2 * BNC * kConvBK * 4;
-  static constexpr int kAccCols = 2 * BNC;
-  static constexpr int kACol0 = 2 * kAccCols;
-  static constexpr int kAStageCols = 2 * kConvBK;
-  static constexpr int kTmemCols = 512;
-  static constexpr int kBarrierBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kBStages * kBStageBytes + kBarrierBytes + BNC * 20;
-};
-
-// Roles (warp index):
-//   [0, kProducerWarps)   A gather: group g = warp/4 fills TMEM A stage g for
-//                         work items g, g+S, ...; warp%4 selects the lane
-//                         quadrant (32 pixel rows), each thread one row x 32 k;
-//   kTmaWarp              streams the [W'_hi; W'_lo] k-slabs into an 8-deep
-//                         shared-memory ring ahead of the MMA;
-//   kMmaWarp              tcgen05.mma with A from TMEM, B from shared memory;
-//   the 4 warps after it  epilogue.
-template <int S, bool kFastC, int kAct>
-__global__ void __launch_bounds__(ConvTmemATraits<S>::kThreads, 1)
-    conv_igemm_tmem_a_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
-  using T = ConvTmemATraits<S>;
-  constexpr int BNC = T::BNC;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
-  uint8_t *smem_b = smem;
-  uint64_t *full_a = reinterpret_cast<uint64_t *>(smem_b + T::kBStages * T::kBStageBytes);
-  uint64_t *empty_a = full_a + T::kStages;
-  uint64_t *full_b = empty_a + T::kStages;
-  uint64_t *empty_b = full_b + T::kBStages;
-  uint64_t *acc_full = empty_b + T::kBStages;
-  uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  float4 *ep_s = reinterpret_cast<float4 *>(smem_b + T::kBStages * T::kBStageBytes +
-                                            T::kBarrierBytes);
-  float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < T::kStages; ++s) {
-      mbar_init(&full_a[s], T::kGroupWarps);
-      mbar_init(&empty_a[s], 1);
-    }
-    for (int s = 0; s < T::kBStages; ++s) {
-      mbar_init(&full_b[s], 1);
-      mbar_init(&empty_b[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&map_w);
-  }
-  if (warp == T::kMmaWarp) {
-    tmem_alloc(tmem_slot, T::kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before_sync();
-  __syncthreads();
-  tc_fence_after_sync();
-  const uint32_t tmem_base = *tmem_slot;
-  const int num_tiles = p.m_blocks * p.n_blocks;
-  const int my_tiles = num_tiles > static_cast<int>(blockIdx.x)
-                           ? (num_tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
-                           : 0;
-  const int items = my_tiles * p.k_blocks;
-
-  if (warp < T::kProducerWarps) {
-    // ---------------- A gather into TMEM ----------------
-    const int group = warp / T::kGroupWarps;
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const int stage = group;
-    const uint32_t t_a = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                         static_cast<uint32_t>(T::kACol0 + stage * T::kAStageCols);
-    uint32_t phase = 0;
-    int cur_tile = -1;
-    int ih0 = 0, iw0 = 0;
-    bool valid = false;
-    const float *xb = p.x;
-    for (int it = group; it < items; it += T::kStages) {
-      const int lt = it / p.k_blocks;
-      const int kb = it - lt * p.k_blocks;
-      const int tile = blockIdx.x + lt * gridDim.x;
-      if (tile != cur_tile) {
-        cur_tile = tile;
-        const int mb = tile / p.n_blocks;
-        const int m = mb * kConvBM + row;
-        valid = m < p.M;
-        int n = 0, oh = 0, ow = 0;
-        if (valid) {
-          n = m / static_cast<int>(p.HoWo);
-          const int pix = m - n * static_cast<int>(p.HoWo);
-          oh = pix / p.Wo;
-          ow = pix - oh * p.Wo;
-        }
-        ih0 = oh * p.sh - p.pt;
-        iw0 = ow * p.sw - p.pl;
-        xb = p.x + static_cast<int64_t>(n) * p.CHW;
-      }
-      float v[32];
-      if (kFastC) {
-        const int taps = p.KH * p.KW;
-        const int cb = kb / taps;
-        const int tap = kb - cb * taps;
-        const int kh = tap / p.KW;
-        const int kw = tap - kh * p.KW;
-        const int ih = ih0 + kh * p.dh, iw = iw0 + kw * p.dw;
-        const bool ok = valid && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
-                        static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
-        const float *base = xb + static_cast<int64_t>(cb * kConvBK) * p.HW +
-                            static_cast<int64_t>(ih) * p.W + iw;
-        if (ok) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __ldg(base + static_cast<int64_t>(j) * p.HW);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.0f;
-        }
-      } else {
-        int k = kb * kConvBK;
-        int tap = k / p.C;
-        int ci = k - tap * p.C;
-        int kh = tap / p.KW;
-        int kw = tap - kh * p.KW;
-        int ih = ih0 + kh * p.dh, iw = iw0 + kw * p.dw;
-        bool ok = valid && kh < p.KH && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
-                  static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
-        const float *ptr =
-            xb + static_cast<int64_t>(ci) * p.HW + static_cast<int64_t>(ih) * p.W + iw;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          v[j] = ok ? __ldg(ptr) : 0.0f;
-          ptr += p.HW;
-          if (++ci == p.C) {
-            ci = 0;
-            if (++kw == p.KW) {
-              kw = 0;
-              ++kh;
-            }
-            ih = ih0 + kh * p.dh;
-            iw = iw0 + kw * p.dw;
-            ok = valid && kh < p.KH && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
-                 static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
-            ptr = xb + static_cast<int64_t>(ih) * p.W + iw;
-          }
-        }
-      }
-      // hi = truncated tf32 part, lo = v - hi (exact); v is dead afterwards.
-      uint32_t hi[32], lo[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float h, l;
-        tf32_split_trunc(v[j], h, l);
-        hi[j] = __float_as_uint(h);
-        lo[j] = __float_as_uint(l);
-      }
-      if (!mbar_wait(&empty_a[stage], phase ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+      if (!conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb, nb,
+                                         ep_s, ep_beta_s, &acc_full[acc], acc_phase, abort_flag))
         break;
-      tc_fence_after_sync();
-      tmem_st32(t_a, hi);
-      tmem_st32(t_a + kConvBK, lo);
-      tmem_wait_st();
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full_a[stage]);
-      phase ^= 1u;
-    }
-  } else if (warp == T::kTmaWarp) {
-    // ---------------- weight slabs, up to kBStages ahead ----------------
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      for (int it = 0; it < items; ++it) {
-        const int lt = it / p.k_blocks;
-        const int kb = it - lt * p.k_blocks;
-        const int tile = blockIdx.x + lt * gridDim.x;
-        const int nb = tile % p.n_blocks;
-        if (!mbar_wait(&empty_b[stage], phase ^ 1u, abort_flag, p.status,
-                       kStatusTimeoutProducer))
-          break;
-        mbar_arrive_expect_tx(&full_b[stage], T::kBStageBytes);
-        tma_load_2d(&map_w, &full_b[stage], smem_b + stage * T::kBStageBytes, kb * kConvBK,
-                    nb * 2 * BNC);
-        if (++stage == T::kBStages) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      }
-    }
-  } else if (warp == T::kMmaWarp) {
-    // ---------------- MMA issuer (A from TMEM, B from shared memory) ----------------
-    if (lane == 0) {
-      const uint32_t idesc_2n = umma_idesc_tf32(kConvBM, 2 * BNC);
-      const uint32_t idesc_n = umma_idesc_tf32(kConvBM, BNC);
-      const uint64_t b_desc0 = umma_desc_sw128(smem_u32(smem_b));
-      int sa = 0, sb = 0;
-      uint32_t pa = 0, pb = 0;
-      int local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
-                       kStatusTimeoutAccFree))
-          break;
-        tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + acc * T::kAccCols;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&full_b[sb], pb, abort_flag, p.status, kStatusTimeoutMma))
-            goto mma_done;
-          if (!mbar_wait(&full_a[sa], pa, abort_flag, p.status, kStatusTimeoutMma))
-            goto mma_done;
-          tc_fence_after_sync();
-          const uint32_t a_col = tmem_base + T::kACol0 + sa * T::kAStageCols;
-          const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(sb * (T::kBStageBytes >> 4));
-#pragma unroll
-          for (int kk = 0; kk < kConvBK / 8; ++kk) {
-            mma_tf32_ts(d_tmem, a_col + kk * 8, b_desc + 2 * kk, idesc_2n,
-                        (kb > 0 || kk > 0) ? 1u : 0u);
-            mma_tf32_ts(d_tmem, a_col + kConvBK + kk * 8, b_desc + 2 * kk, idesc_n, 1u);
-          }
-          mma_commit(&empty_a[sa]);
-          mma_commit(&empty_b[sb]);
-          if (++sa == T::kStages) {
-            sa = 0;
-            pa ^= 1u;
-          }
-          if (++sb == T::kBStages) {
-            sb = 0;
-            pb ^= 1u;
-          }
-        }
-        mma_commit(&acc_full[acc]);
-      }
-    mma_done:;
-    }
-  } else {
-    // ---------------- epilogue (4 warps, one per TMEM lane quadrant) ----------------
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const int et = threadIdx.x - (T::kMmaWarp + 1) * 32;
-    int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      const int mb = tile / p.n_blocks;
-      const int nb = tile - mb * p.n_blocks;
-      mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
-      named_barrier_sync(1, 128);
-      if (*abort_flag) break;
-      for (int i = et; i < BNC; i += 128) {
-        const int co = nb * BNC + i;
-        ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
-                              p.ep[kEpGamma * p.cout_pad + co],
-                              p.ep[kEpInvStd * p.cout_pad + co]);
-        ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
-      }
-      named_barrier_sync(1, 128);
-      tc_fence_after_sync();
-      const int m = mb * kConvBM + row;
-      const bool valid = m < p.M;
-      int n = 0, pix = 0;
-      if (valid) {
-        n = m / static_cast<int>(p.HoWo);
-        pix = m - n * static_cast<int>(p.HoWo);
-      }
-      float *yb = p.y + static_cast<int64_t>(n) * p.Cout * p.HoWo + pix;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * T::kAccCols);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BNC; c0 += 16) {
-        uint32_t v[16], w[16];
-        tmem_ld16(t_row + c0, v);
-        tmem_ld16(t_row + BNC + c0, w);
-        tmem_wait_ld16x2(v, w);
-        const int co0 = nb * BNC + c0;
-        if (valid) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (co0 + 16 > p.Cout && co0 + j >= p.Cout) continue;
-            const float4 q = ep_s[c0 + j];
-            float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
-            t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
-            yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
-          }
-        }
-      }
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -773,11 +364,56 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
 
 namespace {
 
+// Kernel that runs a geometry given the full workspace.
+enum ConvPath {
+  kPathDirect = 0,  // direct NCHW gather (conv_igemm_3xtf32_kernel)
+  kPathIm2col = 1,  // NHWC hi/lo planes + im2col TMA per k-block (conv_im2col.cu)
+  kPathWindow = 2,  // raw NHWC plane + im2col TMA windows shared by the KW taps (conv_window.cu)
+};
+
+// Workspace layout: [W' split: w_bytes][epilogue constants: ep_bytes], then
+// the NHWC input planes: x_hi and x_lo (im2col path) or raw x (window path).
 struct ConvPlan {
   int bnc;
   int64_t kp, n_blocks, cout_pad;
   size_t w_bytes, ep_bytes;
+  int path;
+  int planes;          // NHWC planes the path stages (0, 1 or 2)
+  size_t plane_bytes;  // bytes of one plane
+  size_t min_bytes() const { return w_bytes + ep_bytes; }
+  size_t full_bytes() const { return w_bytes + ep_bytes + planes * plane_bytes; }
 };
+
+// Kernel parameters that depend on the geometry only.
+ConvParams conv_params(const nplk_conv_geom_t *g, const ConvPlan &c) {
+  ConvParams prm{};
+  prm.C = static_cast<int>(g->c_in);
+  prm.H = static_cast<int>(g->h);
+  prm.W = static_cast<int>(g->w);
+  prm.Cout = static_cast<int>(g->c_out);
+  prm.KH = static_cast<int>(g->kh);
+  prm.KW = static_cast<int>(g->kw);
+  prm.sh = static_cast<int>(g->stride_h);
+  prm.sw = static_cast<int>(g->stride_w);
+  prm.pt = static_cast<int>(g->pad_top);
+  prm.pl = static_cast<int>(g->pad_left);
+  prm.dh = static_cast<int>(g->dil_h);
+  prm.dw = static_cast<int>(g->dil_w);
+  prm.Ho = static_cast<int>(g->h_out);
+  prm.Wo = static_cast<int>(g->w_out);
+  prm.HW = g->h * g->w;
+  prm.HoWo = g->h_out * g->w_out;
+  prm.CHW = g->c_in * g->h * g->w;
+  prm.M = static_cast<int>(g->n * g->h_out * g->w_out);
+  prm.Wv = prm.Wo;
+  prm.Mv = prm.M;
+  prm.K = static_cast<int>(g->c_in * g->kh * g->kw);
+  prm.k_blocks = static_cast<int>(c.kp / kConvBK);
+  prm.m_blocks = static_cast<int>(ceil_div(prm.M, kConvBM));
+  prm.n_blocks = static_cast<int>(c.n_blocks);
+  prm.cout_pad = static_cast<int>(c.cout_pad);
+  return prm;
+}
 
 ConvPlan plan_conv(const nplk_conv_geom_t *g) {
   ConvPlan c{};
@@ -788,6 +424,18 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g) {
   c.cout_pad = c.n_blocks * c.bnc;
   c.w_bytes = align_up(static_cast<size_t>(c.cout_pad) * 2 * c.kp * 4, 256);
   c.ep_bytes = align_up(static_cast<size_t>(kEpCount) * c.cout_pad * 4, 256);
+  c.path = kPathDirect;
+  c.planes = 0;
+  c.plane_bytes = align_up(static_cast<size_t>(g->n * g->h * g->w * g->c_in) * 4, 256);
+  const ConvParams prm = conv_params(g, c);
+  const int n = static_cast<int>(g->n);
+  if (g->stride_w == 1 && g->kw > 1 && conv_window_supported(prm, n)) {
+    c.path = kPathWindow;
+    c.planes = 1;
+  } else if (conv_im2col_supported(prm, n)) {
+    c.path = kPathIm2col;
+    c.planes = 2;
+  }
   return c;
 }
 
@@ -808,40 +456,6 @@ int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvPara
   return launch_result();
 }
 
-template <int S, bool kFastC, int kAct>
-int launch_conv_tmem_a(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
-  using T = ConvTmemATraits<S>;
-  CUtensorMap map_w;
-  int rc = encode_tmap_2d_f32_sw128(&map_w, wsplit, c.kp, c.n_blocks * 2 * T::BNC, c.kp * 4,
-                                    kConvBK, 2 * T::BNC);
-  if (rc) return rc;
-  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(conv_igemm_tmem_a_kernel<S, kFastC, kAct>),
-                           T::kSmemBytes);
-  if (rc) return rc;
-  const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
-  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_igemm_tmem_a_kernel<S, kFastC, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm);
-  count_launch();
-  return launch_result();
-}
-
-template <bool kFastC>
-int dispatch_act_tmem_a(cudaStream_t s, const ConvPlan &c, const float *wsplit,
-                        const ConvParams &prm) {
-  constexpr int S = kConvTmemAStages;
-  if (prm.act == 0) return launch_conv_tmem_a<S, kFastC, kEpiActNone>(s, c, wsplit, prm);
-  if (prm.act == 1) return launch_conv_tmem_a<S, kFastC, kEpiActRelu>(s, c, wsplit, prm);
-  return launch_conv_tmem_a<S, kFastC, kEpiActAny>(s, c, wsplit, prm);
-}
-
-bool tmem_a_enabled() {
-  static const bool on = [] {
-    const char *e = std::getenv("NPL_CONV_A_IN_TMEM");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
-
 template <int BNC, bool kFastC>
 int dispatch_act(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
   if (prm.act == 0) return launch_conv<BNC, kFastC, kEpiActNone>(s, c, wsplit, prm);
@@ -851,9 +465,6 @@ int dispatch_act(cudaStream_t s, const ConvPlan &c, const float *wsplit, const C
 
 int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm,
                   bool fast) {
-  if (c.bnc == 64 && tmem_a_enabled())
-    return fast ? dispatch_act_tmem_a<true>(s, c, wsplit, prm)
-                : dispatch_act_tmem_a<false>(s, c, wsplit, prm);
   if (c.bnc == 64)
     return fast ? dispatch_act<64, true>(s, c, wsplit, prm)
                 : dispatch_act<64, false>(s, c, wsplit, prm);
@@ -884,8 +495,12 @@ using namespace nplk;
 
 extern "C" size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g) {
   if (validate_conv_geom(g) != kOk) return 0;
-  const ConvPlan c = plan_conv(g);
-  return c.w_bytes + c.ep_bytes;
+  return plan_conv(g).full_bytes();
+}
+
+extern "C" size_t nplk_conv_workspace_min_size(const nplk_conv_geom_t *g) {
+  if (validate_conv_geom(g) != kOk) return 0;
+  return plan_conv(g).min_bytes();
 }
 
 namespace {
@@ -896,7 +511,7 @@ int check_conv_call(const nplk_conv_geom_t *g, void *workspace, size_t workspace
   int rc = validate_conv_geom(g);
   if (rc) return rc;
   *c = plan_conv(g);
-  if (!workspace || workspace_bytes < c->w_bytes + c->ep_bytes ||
+  if (!workspace || workspace_bytes < c->min_bytes() ||
       (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return kErrInvalidArg;
   return kOk;
@@ -928,50 +543,89 @@ extern "C" int nplk_conv2d_prepare(void *stream, const nplk_conv_geom_t *g, cons
   return launch_result();
 }
 
-extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
-                               int act, float act_alpha, float *out, const void *workspace,
-                               size_t workspace_bytes, int *status) {
-  ConvPlan c;
-  int rc = check_conv_call(g, const_cast<void *>(workspace), workspace_bytes, &c);
+namespace {
+
+// Everything run needs besides x: validated plan, status word and the
+// geometry-dependent kernel parameters.
+int begin_run(const nplk_conv_geom_t *g, void *workspace, size_t workspace_bytes, int act,
+              float act_alpha, float *out, int *status, ConvPlan *c, ConvParams *prm) {
+  int rc = check_conv_call(g, workspace, workspace_bytes, c);
   if (rc) return rc;
-  if (!x || !out) return kErrInvalidArg;
+  if (!out) return kErrInvalidArg;
   if (!status) status = device_status_word();
   if (!status) return kErrInternal;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const float *wsplit = static_cast<const float *>(workspace);
-  const float *ep =
-      reinterpret_cast<const float *>(static_cast<const uint8_t *>(workspace) + c.w_bytes);
-  ConvParams prm{};
+  *prm = conv_params(g, *c);
+  prm->y = out;
+  prm->ep = reinterpret_cast<const float *>(static_cast<const uint8_t *>(workspace) + c->w_bytes);
+  prm->act = act;
+  prm->act_alpha = act_alpha;
+  prm->status = status;
+  return kOk;
+}
+
+float *plane_hi(void *workspace, const ConvPlan &c) {
+  return reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + c.min_bytes());
+}
+
+float *plane_lo(void *workspace, const ConvPlan &c) {
+  return reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + c.min_bytes() +
+                                   c.plane_bytes);
+}
+
+bool has_planes(const ConvPlan &c, size_t workspace_bytes) {
+  return c.planes > 0 && workspace_bytes >= c.full_bytes();
+}
+
+}  // namespace
+
+extern "C" int nplk_conv2d_stage_input(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                       void *workspace, size_t workspace_bytes) {
+  ConvPlan c;
+  int rc = check_conv_call(g, workspace, workspace_bytes, &c);
+  if (rc) return rc;
+  if (!x) return kErrInvalidArg;
+  if (!has_planes(c, workspace_bytes)) return kErrUnsupported;
+  return launch_nchw_to_nhwc_split(static_cast<cudaStream_t>(stream), x, plane_hi(workspace, c),
+                                   c.planes == 2 ? plane_lo(workspace, c) : nullptr,
+                                   static_cast<int>(g->n), static_cast<int>(g->c_in), g->h * g->w);
+}
+
+extern "C" int nplk_conv2d_run_staged(void *stream, const nplk_conv_geom_t *g, int act,
+                                      float act_alpha, float *out, void *workspace,
+                                      size_t workspace_bytes, int *status) {
+  ConvPlan c;
+  ConvParams prm;
+  int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
+  if (rc) return rc;
+  if (!has_planes(c, workspace_bytes)) return kErrUnsupported;
+  if (c.path == kPathWindow)
+    return launch_conv_window(static_cast<cudaStream_t>(stream), c.bnc,
+                              static_cast<const float *>(workspace), c.kp, c.n_blocks,
+                              plane_hi(workspace, c), prm, static_cast<int>(g->n));
+  return launch_conv_im2col(static_cast<cudaStream_t>(stream), c.bnc,
+                            static_cast<const float *>(workspace), c.kp, c.n_blocks,
+                            plane_hi(workspace, c), plane_lo(workspace, c), prm,
+                            static_cast<int>(g->n));
+}
+
+extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
+                               int act, float act_alpha, float *out, void *workspace,
+                               size_t workspace_bytes, int *status) {
+  ConvPlan c;
+  ConvParams prm;
+  int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
+  if (rc) return rc;
+  if (!x) return kErrInvalidArg;
+  if (has_planes(c, workspace_bytes)) {
+    // TMA paths: NHWC plane(s), then the conv kernel.
+    rc = nplk_conv2d_stage_input(stream, g, x, workspace, workspace_bytes);
+    if (rc) return rc;
+    return nplk_conv2d_run_staged(stream, g, act, act_alpha, out, workspace, workspace_bytes,
+                                  prm.status);
+  }
   prm.x = x;
-  prm.y = out;
-  prm.C = static_cast<int>(g->c_in);
-  prm.H = static_cast<int>(g->h);
-  prm.W = static_cast<int>(g->w);
-  prm.Cout = static_cast<int>(g->c_out);
-  prm.KH = static_cast<int>(g->kh);
-  prm.KW = static_cast<int>(g->kw);
-  prm.sh = static_cast<int>(g->stride_h);
-  prm.sw = static_cast<int>(g->stride_w);
-  prm.pt = static_cast<int>(g->pad_top);
-  prm.pl = static_cast<int>(g->pad_left);
-  prm.dh = static_cast<int>(g->dil_h);
-  prm.dw = static_cast<int>(g->dil_w);
-  prm.Ho = static_cast<int>(g->h_out);
-  prm.Wo = static_cast<int>(g->w_out);
-  prm.HW = g->h * g->w;
-  prm.HoWo = g->h_out * g->w_out;
-  prm.CHW = g->c_in * g->h * g->w;
-  prm.M = static_cast<int>(g->n * g->h_out * g->w_out);
-  prm.K = static_cast<int>(g->c_in * g->kh * g->kw);
-  prm.k_blocks = static_cast<int>(c.kp / kConvBK);
-  prm.m_blocks = static_cast<int>(ceil_div(prm.M, kConvBM));
-  prm.n_blocks = static_cast<int>(c.n_blocks);
-  prm.ep = ep;
-  prm.cout_pad = static_cast<int>(c.cout_pad);
-  prm.act = act;
-  prm.act_alpha = act_alpha;
-  prm.status = status;
-  return dispatch_conv(s, c, wsplit, prm, g->c_in % kConvBK == 0);
+  return dispatch_conv(static_cast<cudaStream_t>(stream), c,
+                       static_cast<const float *>(workspace), prm, g->c_in % kConvBK == 0);
 }
 
 extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,

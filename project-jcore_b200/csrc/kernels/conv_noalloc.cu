@@ -12,8 +12,10 @@
 //
 // Properties a caller must know:
 //   * Capacity: the array holds kNoAllocScratchBytes (8 MiB). Geometries whose
-//     workspace would exceed it are rejected with NPL_ERR_UNSUPPORTED and a
-//     message on stderr.
+//     minimum workspace (split weights + epilogue constants) would exceed it
+//     are rejected with NPL_ERR_UNSUPPORTED and a message on stderr. When the
+//     full workspace (which adds the NHWC input planes) does not fit, the
+//     conv runs on the direct-gather kernel, with identical results.
 //   * Footprint: every GPU on which the library is loaded keeps the 8 MiB
 //     (plus one status word) until the process exits.
 //   * Set-up: the first call on each device looks up the array's device
@@ -88,7 +90,7 @@ extern "C" int nplk_conv2d_fused_noalloc(void *stream, const nplk_conv_geom_t *g
                                          float bn_eps, int act, float act_alpha, float *out,
                                          int *status) {
   if (!g || !x || !w || !out) return kErrInvalidArg;
-  const size_t need = nplk_conv_workspace_size(g);
+  const size_t need = nplk_conv_workspace_min_size(g);
   if (need == 0) return kErrInvalidArg;
   if (need > kNoAllocScratchBytes) {
     std::fprintf(stderr,

@@ -45,6 +45,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   }();
   return fn;
 }
+
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  }();
+  return fn;
+}
 }  // namespace
 
 int sm_count() {
@@ -105,6 +119,25 @@ int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kErrInternal;
+}
+
+int encode_tmap_im2col_nhwc_f32_sw128(CUtensorMap *map, const void *base, uint64_t c,
+                                     uint64_t w, uint64_t h, uint64_t n, int lower_w,
+                                     int lower_h, int upper_w, int upper_h, uint32_t stride_w,
+                                     uint32_t stride_h, uint32_t channels, uint32_t pixels) {
+  auto fn = encode_im2col_fn();
+  if (!fn) return kErrInternal;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (c * 4) % 16 != 0) return kErrInvalidArg;
+  cuuint64_t dims[4] = {c, w, h, n};
+  cuuint64_t strides[3] = {c * 4, c * w * 4, c * w * h * 4};
+  int lower[2] = {lower_w, lower_h};
+  int upper[2] = {upper_w, upper_h};
+  cuuint32_t estr[4] = {1, stride_w, stride_h, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims,
+                  strides, lower, upper, channels, pixels, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? kOk : kErrInternal;

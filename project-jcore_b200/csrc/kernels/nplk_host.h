@@ -45,6 +45,16 @@ int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
                              uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
                              uint32_t box_outer);
 
+// 4-D NHWC fp32 im2col tensor map (dims {c, w, h, n}, densely packed): each
+// load gathers `pixels` output pixels x `channels` channels, walking the
+// bounding box [lower, dim-1+upper] of every image with the given traversal
+// strides (W then H then N); corners are in [-128, 127]. 128-byte swizzle,
+// zero fill outside the image.
+int encode_tmap_im2col_nhwc_f32_sw128(CUtensorMap *map, const void *base, uint64_t c,
+                                     uint64_t w, uint64_t h, uint64_t n, int lower_w,
+                                     int lower_h, int upper_w, int upper_h, uint32_t stride_w,
+                                     uint32_t stride_h, uint32_t channels, uint32_t pixels);
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

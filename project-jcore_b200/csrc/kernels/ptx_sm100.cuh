@@ -94,6 +94,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait that ignores the abort flag: on the way out of an aborted CTA
+// the TMA producer waits here for the copies it issued into shared memory, so
+// that none lands after the CTA has exited. Returns false after
+// kDrainLimitNs.
+constexpr uint64_t kDrainLimitNs = 100000000ull;
+__device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > kDrainLimitNs) return false;
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // Progress counter in shared memory. An mbarrier wait costs the MMA-issuing
 // thread ~130-200 cycles even when the phase is already complete, which
@@ -152,6 +165,21 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, uint64_t *ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// 4-D im2col load (NHWC tensor map from cuTensorMapEncodeIm2col): gathers the
+// map's pixels-per-column output pixels starting at input position (w, h) of
+// image n, each shifted by the filter offset (off_w, off_h), channels
+// [c, c + channels-per-pixel). Positions outside the image read as zero.
+__device__ __forceinline__ void tma_load_im2col_4d(const CUtensorMap *map, uint64_t *bar,
+                                                   void *dst, int c, int w, int h, int n,
+                                                   uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n),
+      "h"(off_w), "h"(off_h)
       : "memory");
 }
 

@@ -160,11 +160,14 @@ NPLK_SIGNATURES = {
     "nplk_gemm": (C.c_int, [_VP, _I64, _I64, _I64, _F, _VP, _I64, _VP, _I64, _F, _VP, _I64,
                             _VP, C.c_int, _F, C.c_uint, _VP, C.c_size_t, _VP]),
     "nplk_conv_workspace_size": (C.c_size_t, [_G]),
+    "nplk_conv_workspace_min_size": (C.c_size_t, [_G]),
     "nplk_conv2d_fused": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, C.c_int,
                                     _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_conv2d_prepare": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP,
                                       C.c_size_t]),
     "nplk_conv2d_run": (C.c_int, [_VP, _G, _VP, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
+    "nplk_conv2d_stage_input": (C.c_int, [_VP, _G, _VP, _VP, C.c_size_t]),
+    "nplk_conv2d_run_staged": (C.c_int, [_VP, _G, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_conv2d_fused_noalloc": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
                                             C.c_int, _F, _VP, _VP]),
     "nplk_depthwise_conv2d": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP]),
