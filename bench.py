@@ -5,9 +5,10 @@ Workload (one "step"): npl_conv2d_bn_activation on the ResNet-style 3x3 layer
 N=32, C_in=64, H=W=56, C_out=64, stride 1, pad 1, no bias, inference BN
 (gamma U[0.5,1.5], beta U[-0.1,0.1], mean N(0,0.1), var U[0.5,1.5], eps 1e-5),
 ReLU; input U[0,1], weights N(0, sqrt(2/576)). Synthetic seeded inputs.
-A step is the full operator: weight preparation (tf32 split + BN constants),
-the input's rewrite as NHWC tf32 hi/lo planes and the fused implicit-GEMM
-conv kernel (A tiles by im2col-mode TMA). At N GPUs every rank runs its own
+A step is the full operator: weight preparation (tf32 split + BN constants)
+and the fused implicit-GEMM conv kernel the library picks for the geometry
+(for this 3x3 stride-1 layer: shared im2col windows gathered from NCHW x,
+two MMA pipelines per CTA). At N GPUs every rank runs its own
 batch of 32 (batch-sharded data parallelism, no collective): weak scaling.
 
 Reported (one JSON line on rank 0):
@@ -225,25 +226,20 @@ def run_b200(args, rank, world, local_rank):
                                     1e-5, p(work), ws)
         assert r == 0, r
 
-    def stage():
-        r = lib.nplk_conv2d_stage_input(sptr, C.byref(g), p(tx), p(work), ws)
-        assert r == 0, r
-
     def run():
-        r = lib.nplk_conv2d_run_staged(sptr, C.byref(g), nb.NPL_ACT_RELU, 0.0, p(ty), p(work),
-                                       ws, None)
+        r = lib.nplk_conv2d_run(sptr, C.byref(g), p(tx), nb.NPL_ACT_RELU, 0.0, p(ty), p(work),
+                                ws, None)
         assert r == 0, r
 
     for _ in range(args.warmup):
         flush.zero_()
         prepare()
-        stage()
         run()
     torch.cuda.synchronize()
     if lib.nplk_read_status(sptr) != 0:
         raise RuntimeError("conv kernel reported a pipeline timeout")
 
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if world > 1:
         dist.barrier()
@@ -256,10 +252,8 @@ def run_b200(args, rank, world, local_rank):
         ev[i][0].record(stream)
         prepare()
         ev[i][1].record(stream)
-        stage()
-        ev[i][2].record(stream)
         run()
-        ev[i][3].record(stream)
+        ev[i][2].record(stream)
     torch.cuda.synchronize()
     launches = int(lib.nplk_take_launch_count())
     if world > 1:
@@ -267,16 +261,15 @@ def run_b200(args, rank, world, local_rank):
     clocks = sampler.stop() if sampler else None
     if lib.nplk_read_status(sptr) != 0:
         raise RuntimeError("conv kernel reported a pipeline timeout")
-    step_ms = [e[0].elapsed_time(e[3]) for e in ev]
-    stage_ms = [e[1].elapsed_time(e[2]) for e in ev]
-    conv_ms = [e[2].elapsed_time(e[3]) for e in ev]
-    stats = torch.tensor([sum(step_ms) / len(step_ms), statistics.mean(conv_ms),
-                          statistics.mean(stage_ms)], device=dev, dtype=torch.float64)
+    step_ms = [e[0].elapsed_time(e[2]) for e in ev]
+    conv_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    stats = torch.tensor([sum(step_ms) / len(step_ms), statistics.mean(conv_ms)],
+                         device=dev, dtype=torch.float64)
     tot_launch = torch.tensor([launches], device=dev, dtype=torch.int64)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         dist.all_reduce(tot_launch, op=dist.ReduceOp.SUM)
-    ms_per_step, conv_kernel_ms, stage_kernel_ms = stats.tolist()
+    ms_per_step, conv_kernel_ms = stats.tolist()
 
     # ---- e2e through the public C ABI with pinned host buffers ----
     hx = torch.from_numpy(x).pin_memory()
@@ -320,7 +313,7 @@ def run_b200(args, rank, world, local_rank):
         tf32x3_peak = bf16_peak / 2.0 / 3.0
         achieved = (CONV_FLOPS / 1e12) / (conv_kernel_ms / 1e3)
         traffic = None
-        tp = REPO / "profiles" / "conv_im2col_traffic.json"
+        tp = REPO / "profiles" / "conv_window_traffic.json"
         if tp.exists():
             traffic = json.loads(tp.read_text()).get("dram_bytes_per_launch")
         value = world * CONV_FLOPS / (ms_per_step / 1e3) / 1e12
@@ -343,8 +336,7 @@ def run_b200(args, rank, world, local_rank):
                 "global_batch": N_IMG * world,
                 "parallelism": f"dp{world} (batch-sharded, no collective)",
                 "l2": "flushed between steps (256 MiB write, outside the timed events)",
-                "step": "nplk_conv2d_prepare (weight split + BN constants) + "
-                        "nplk_conv2d_stage_input (NHWC hi/lo planes) + nplk_conv2d_run_staged",
+                "step": "nplk_conv2d_prepare (weight split + BN constants) + nplk_conv2d_run",
             },
             "e2e": {
                 "value": round(world * CONV_FLOPS / e2e_step / 1e12, 3),
@@ -360,11 +352,8 @@ def run_b200(args, rank, world, local_rank):
                 "unit": "TFLOP/s",
                 "frac": round(achieved / tf32x3_peak, 4),
                 "traffic": traffic,
-                "kernel": "conv_im2col_3xtf32_kernel<64>",
+                "kernel": "conv_window_3xtf32_kernel<64, relu, gather>",
                 "kernel_ms": round(conv_kernel_ms, 5),
-                "stage_kernel_ms": round(stage_kernel_ms, 5),
-                "stage_gbs": round(3 * N_IMG * C_IN * HW_IN * HW_IN * 4 / (stage_kernel_ms / 1e3)
-                                   / 1e9, 1),
                 "peak_basis": f"{peak_src} bf16 {bf16_peak} TFLOP/s / 2 (TF32) / 3 (3xTF32)",
             },
             "gpu_launches": int(tot_launch.item()),

@@ -79,6 +79,27 @@ typedef struct {
  * and lo parts) that the fastest kernel reads. */
 NPL_API size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g);
 
+/* Conv kernels (all compute the same products in the same order, so their
+ * results are identical bit for bit):
+ *   DIRECT         gathers x (NCHW) per k-block into shared memory; any geometry;
+ *   IM2COL         NHWC tf32 hi/lo planes of x, one im2col TMA load per k-block;
+ *                  C_in % 32 == 0;
+ *   WINDOW         raw NHWC plane of x, one im2col TMA window per (tile, channel
+ *                  block, filter row) shared by the filter columns (stride_w 1);
+ *   WINDOW_GATHER  the same windows gathered from NCHW x inside the conv kernel
+ *                  (no planes, one launch). AUTO picks the fastest that applies. */
+enum {
+  NPLK_CONV_ALGO_AUTO = 0,
+  NPLK_CONV_ALGO_DIRECT = 1,
+  NPLK_CONV_ALGO_IM2COL = 2,
+  NPLK_CONV_ALGO_WINDOW = 3,
+  NPLK_CONV_ALGO_WINDOW_GATHER = 4
+};
+
+/* Workspace bytes of nplk_conv2d_run_algo with `algo`; 0 when the geometry
+ * does not suit that kernel. */
+NPL_API size_t nplk_conv_workspace_size_algo(const nplk_conv_geom_t *g, int algo);
+
 /* Smallest workspace the conv entry points accept (split weights and
  * epilogue constants only). With less than nplk_conv_workspace_size bytes
  * the conv runs on the direct-gather kernel, which reads NCHW x itself; the
@@ -114,9 +135,16 @@ NPL_API int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float
                             float act_alpha, float *out, void *workspace,
                             size_t workspace_bytes, int *status);
 
-/* nplk_conv2d_run in two steps, for the TMA-im2col path only (geometries
- * where nplk_conv_workspace_size exceeds nplk_conv_workspace_min_size, with
- * the full workspace): stage_input rewrites x as the NHWC tf32 hi/lo planes
+/* nplk_conv2d_run with a given kernel (NPLK_CONV_ALGO_*), for tests and
+ * tuning: NPL_ERR_UNSUPPORTED when the geometry does not suit it,
+ * NPL_ERR_INVALID_ARG when the workspace is below
+ * nplk_conv_workspace_size_algo. */
+NPL_API int nplk_conv2d_run_algo(void *stream, const nplk_conv_geom_t *g, const float *x, int act,
+                                 float act_alpha, float *out, void *workspace,
+                                 size_t workspace_bytes, int *status, int algo);
+
+/* nplk_conv2d_run in two steps, for the kernels that read NHWC planes (the
+ * AUTO choice is IM2COL or WINDOW, with the full workspace): stage_input rewrites x as the NHWC tf32 hi/lo planes
  * in the workspace, run_staged runs the conv kernel on them. One staged input
  * serves any number of run_staged calls of the same geometry (for example
  * two convolutions of one input). Both return NPL_ERR_UNSUPPORTED where the

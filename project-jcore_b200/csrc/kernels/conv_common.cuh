@@ -148,6 +148,8 @@ int launch_nchw_to_nhwc_split(cudaStream_t s, const float *x, float *hi, float *
 int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
                        const float *x_nhwc, ConvParams prm, int n_img);
 bool conv_window_supported(const ConvParams &prm, int n_img);
+// The gather variant also needs x to have fewer than 2^31 elements.
+bool conv_window_gather_supported(const ConvParams &prm, int n_img);
 void conv_window_rows(const ConvParams &p, int *wv, int64_t *mv);
 
 }  // namespace nplk

@@ -369,6 +369,7 @@ enum ConvPath {
   kPathDirect = 0,  // direct NCHW gather (conv_igemm_3xtf32_kernel)
   kPathIm2col = 1,  // NHWC hi/lo planes + im2col TMA per k-block (conv_im2col.cu)
   kPathWindow = 2,  // raw NHWC plane + im2col TMA windows shared by the KW taps (conv_window.cu)
+  kPathWindowGather = 3,  // the same windows gathered from NCHW x by the kernel itself
 };
 
 // Workspace layout: [W' split: w_bytes][epilogue constants: ep_bytes], then
@@ -415,7 +416,11 @@ ConvParams conv_params(const nplk_conv_geom_t *g, const ConvPlan &c) {
   return prm;
 }
 
-ConvPlan plan_conv(const nplk_conv_geom_t *g) {
+// Plan for algorithm `algo` (NPLK_CONV_ALGO_*); path -1 when the geometry
+// does not suit it. AUTO picks the shared-window gather kernel for stride-1
+// filters wider than one column, the per-k-block im2col kernel for the
+// other TMA-eligible geometries and the direct kernel otherwise.
+ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
   ConvPlan c{};
   c.bnc = g->c_out <= 64 ? 64 : 128;
   const int64_t K = g->c_in * g->kh * g->kw;
@@ -424,18 +429,36 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g) {
   c.cout_pad = c.n_blocks * c.bnc;
   c.w_bytes = align_up(static_cast<size_t>(c.cout_pad) * 2 * c.kp * 4, 256);
   c.ep_bytes = align_up(static_cast<size_t>(kEpCount) * c.cout_pad * 4, 256);
-  c.path = kPathDirect;
-  c.planes = 0;
   c.plane_bytes = align_up(static_cast<size_t>(g->n * g->h * g->w * g->c_in) * 4, 256);
   const ConvParams prm = conv_params(g, c);
   const int n = static_cast<int>(g->n);
-  if (g->stride_w == 1 && g->kw > 1 && conv_window_supported(prm, n)) {
-    c.path = kPathWindow;
-    c.planes = 1;
-  } else if (conv_im2col_supported(prm, n)) {
-    c.path = kPathIm2col;
-    c.planes = 2;
+  const bool window_ok = conv_window_supported(prm, n);
+  const bool gather_ok = conv_window_gather_supported(prm, n);
+  const bool im2col_ok = conv_im2col_supported(prm, n);
+  const bool shared_taps = g->stride_w == 1 && g->kw > 1;
+  switch (algo) {
+    case NPLK_CONV_ALGO_AUTO:
+      c.path = (gather_ok && shared_taps)   ? kPathWindowGather
+               : (window_ok && shared_taps) ? kPathWindow
+               : im2col_ok                  ? kPathIm2col
+                                            : kPathDirect;
+      break;
+    case NPLK_CONV_ALGO_DIRECT:
+      c.path = kPathDirect;
+      break;
+    case NPLK_CONV_ALGO_IM2COL:
+      c.path = im2col_ok ? kPathIm2col : -1;
+      break;
+    case NPLK_CONV_ALGO_WINDOW:
+      c.path = window_ok ? kPathWindow : -1;
+      break;
+    case NPLK_CONV_ALGO_WINDOW_GATHER:
+      c.path = gather_ok ? kPathWindowGather : -1;
+      break;
+    default:
+      c.path = -1;
   }
+  c.planes = c.path == kPathIm2col ? 2 : c.path == kPathWindow ? 1 : 0;
   return c;
 }
 
@@ -496,6 +519,12 @@ using namespace nplk;
 extern "C" size_t nplk_conv_workspace_size(const nplk_conv_geom_t *g) {
   if (validate_conv_geom(g) != kOk) return 0;
   return plan_conv(g).full_bytes();
+}
+
+extern "C" size_t nplk_conv_workspace_size_algo(const nplk_conv_geom_t *g, int algo) {
+  if (validate_conv_geom(g) != kOk) return 0;
+  const ConvPlan c = plan_conv(g, algo);
+  return c.path < 0 ? 0 : c.full_bytes();
 }
 
 extern "C" size_t nplk_conv_workspace_min_size(const nplk_conv_geom_t *g) {
@@ -578,6 +607,41 @@ bool has_planes(const ConvPlan &c, size_t workspace_bytes) {
 
 }  // namespace
 
+namespace {
+
+// Runs plan `c` (workspace already checked against c.full_bytes()).
+int run_plan(cudaStream_t s, const nplk_conv_geom_t *g, const float *x, const ConvPlan &c,
+             ConvParams prm, void *workspace, bool stage) {
+  const float *wsplit = static_cast<const float *>(workspace);
+  const int n = static_cast<int>(g->n);
+  switch (c.path) {
+    case kPathWindowGather:
+      prm.x = x;
+      return launch_conv_window(s, c.bnc, wsplit, c.kp, c.n_blocks, nullptr, prm, n);
+    case kPathWindow:
+    case kPathIm2col: {
+      if (stage) {
+        int rc = launch_nchw_to_nhwc_split(s, x, plane_hi(workspace, c),
+                                           c.planes == 2 ? plane_lo(workspace, c) : nullptr, n,
+                                           static_cast<int>(g->c_in), g->h * g->w);
+        if (rc) return rc;
+      }
+      if (c.path == kPathWindow)
+        return launch_conv_window(s, c.bnc, wsplit, c.kp, c.n_blocks, plane_hi(workspace, c), prm,
+                                  n);
+      return launch_conv_im2col(s, c.bnc, wsplit, c.kp, c.n_blocks, plane_hi(workspace, c),
+                                plane_lo(workspace, c), prm, n);
+    }
+    case kPathDirect:
+      prm.x = x;
+      return dispatch_conv(s, c, wsplit, prm, g->c_in % kConvBK == 0);
+    default:
+      return kErrUnsupported;
+  }
+}
+
+}  // namespace
+
 extern "C" int nplk_conv2d_stage_input(void *stream, const nplk_conv_geom_t *g, const float *x,
                                        void *workspace, size_t workspace_bytes) {
   ConvPlan c;
@@ -598,14 +662,7 @@ extern "C" int nplk_conv2d_run_staged(void *stream, const nplk_conv_geom_t *g, i
   int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
   if (rc) return rc;
   if (!has_planes(c, workspace_bytes)) return kErrUnsupported;
-  if (c.path == kPathWindow)
-    return launch_conv_window(static_cast<cudaStream_t>(stream), c.bnc,
-                              static_cast<const float *>(workspace), c.kp, c.n_blocks,
-                              plane_hi(workspace, c), prm, static_cast<int>(g->n));
-  return launch_conv_im2col(static_cast<cudaStream_t>(stream), c.bnc,
-                            static_cast<const float *>(workspace), c.kp, c.n_blocks,
-                            plane_hi(workspace, c), plane_lo(workspace, c), prm,
-                            static_cast<int>(g->n));
+  return run_plan(static_cast<cudaStream_t>(stream), g, nullptr, c, prm, workspace, false);
 }
 
 extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
@@ -616,16 +673,24 @@ extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const fl
   int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
   if (rc) return rc;
   if (!x) return kErrInvalidArg;
-  if (has_planes(c, workspace_bytes)) {
-    // TMA paths: NHWC plane(s), then the conv kernel.
-    rc = nplk_conv2d_stage_input(stream, g, x, workspace, workspace_bytes);
-    if (rc) return rc;
-    return nplk_conv2d_run_staged(stream, g, act, act_alpha, out, workspace, workspace_bytes,
-                                  prm.status);
-  }
-  prm.x = x;
-  return dispatch_conv(static_cast<cudaStream_t>(stream), c,
-                       static_cast<const float *>(workspace), prm, g->c_in % kConvBK == 0);
+  // A workspace too small for the planes of the chosen kernel selects the
+  // direct kernel (same results).
+  if (workspace_bytes < c.full_bytes()) c.path = kPathDirect;
+  return run_plan(static_cast<cudaStream_t>(stream), g, x, c, prm, workspace, true);
+}
+
+extern "C" int nplk_conv2d_run_algo(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                    int act, float act_alpha, float *out, void *workspace,
+                                    size_t workspace_bytes, int *status, int algo) {
+  ConvPlan c;
+  ConvParams prm;
+  int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
+  if (rc) return rc;
+  if (!x) return kErrInvalidArg;
+  c = plan_conv(g, algo);
+  if (c.path < 0) return kErrUnsupported;
+  if (workspace_bytes < c.full_bytes()) return kErrInvalidArg;
+  return run_plan(static_cast<cudaStream_t>(stream), g, x, c, prm, workspace, true);
 }
 
 extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const float *x,

@@ -39,7 +39,7 @@ constexpr int kWinMaxExtra = 8;                                   // (KW-1)*dw l
 constexpr int kWinRowsMax = kConvBM + kWinMaxExtra;               // 136
 constexpr int kWinBytes = kWinRowsMax * kConvBK * 4;              // 17 KB, 1024-aligned
 
-template <int BNC>
+template <int BNC, bool kGather>
 struct ConvWinTraits {
   static constexpr int kPipes = BNC == 64 ? 2 : 1;
   static constexpr int kWinSlots = BNC == 64 ? 2 : 3;  // per pipeline
@@ -47,11 +47,15 @@ struct ConvWinTraits {
   static constexpr int kBBytes = 2 * BNC * kConvBK * 4;
   static constexpr int kWinSlotBytes = 2 * kWinBytes;  // raw + lo
   static constexpr int kPipeBytes = kWinSlots * kWinSlotBytes + kBSlots * kBBytes;
-  // warps [0, 2*kPipes): producers, two per pipeline (windows, weight slabs)
-  static constexpr int kFirstMmaWarp = 2 * kPipes;
-  static constexpr int kFirstCvtWarp = 3 * kPipes;       // 4 converter warps per pipeline
-  static constexpr int kFirstEpiWarp = 7 * kPipes;       // then 4 epilogue warps
-  static constexpr int kThreads = (7 * kPipes + 4) * 32;
+  // warps [0, kProdWarps): TMA producers, per pipeline one for the weight
+  // slabs and (TMA windows only) one for the windows; then one MMA warp per
+  // pipeline, 4 window warps per pipeline (converter or gather), 4 epilogue
+  // warps.
+  static constexpr int kProdWarps = kGather ? kPipes : 2 * kPipes;
+  static constexpr int kFirstMmaWarp = kProdWarps;
+  static constexpr int kFirstCvtWarp = kProdWarps + kPipes;
+  static constexpr int kFirstEpiWarp = kFirstCvtWarp + 4 * kPipes;
+  static constexpr int kThreads = (kFirstEpiWarp + 4) * 32;
   static constexpr int kAccCols = 2 * BNC;
   static constexpr int kAccPerPipe = 2;
   static constexpr int kTmemCols = kPipes * kAccPerPipe * kAccCols;
@@ -67,12 +71,16 @@ struct WinGeom {
   int wins_per_row;  // KW / taps_per_win
 };
 
-template <int BNC, int kAct>
-__global__ void __launch_bounds__(ConvWinTraits<BNC>::kThreads, 1)
+// kGather: the window warpgroups load the window straight from NCHW x
+// (coalesced along w), writing x and lo = x - trunc(x) into the window slot;
+// no NHWC plane, no window TMA. Otherwise the window comes from the raw NHWC
+// plane by im2col TMA and the warpgroups only add the lo part.
+template <int BNC, int kAct, bool kGather>
+__global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     conv_window_3xtf32_kernel(const __grid_constant__ CUtensorMap map_x,
                               const __grid_constant__ CUtensorMap map_w, const ConvParams p,
                               const WinGeom wg) {
-  using T = ConvWinTraits<BNC>;
+  using T = ConvWinTraits<BNC, kGather>;
   constexpr int P = T::kPipes;
   constexpr int WS = T::kWinSlots;
   constexpr int BS = T::kBSlots;
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC>::kThreads, 1)
     }
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&map_x);
+    if (!kGather) tma_prefetch_desc(&map_x);
     tma_prefetch_desc(&map_w);
   }
   if (warp == T::kFirstMmaWarp) {
@@ -129,13 +137,13 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC>::kThreads, 1)
   // runs it. Per tile: windows (cb, kh, kw group) in that order, each
   // followed by its taps_per_win weight slabs.
 
-  if (warp < 2 * P) {
+  if (warp < T::kProdWarps) {
     // ---------------- TMA producers of pipeline `pipe` ----------------
     // Windows and weight slabs come from two threads, so that a window can
     // be requested as soon as its slot is free (a whole window of MMA work
     // ahead), not only after the previous window's slabs were issued.
-    const int pipe = warp >> 1;
-    const bool slabs = (warp & 1) != 0;
+    const int pipe = kGather ? warp : warp >> 1;
+    const bool slabs = kGather || (warp & 1) != 0;
     if (lane == 0) {
       uint8_t *base = smem + pipe * T::kPipeBytes;
       uint8_t *bslots = base + WS * T::kWinSlotBytes;
@@ -262,6 +270,100 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC>::kThreads, 1)
       }
     mma_done:;
     }
+  } else if (warp < T::kFirstEpiWarp && kGather) {
+    // ---------------- gather warpgroup of pipeline `pipe`: window from NCHW x ----------------
+    // Warp gw of the group loads channel quads gw and gw + 4 of the window's
+    // 32 channels; lane l loads rows l, l + 32, ... (consecutive virtual
+    // pixels, so each load instruction reads consecutive input columns).
+    const int pipe = (warp - T::kFirstCvtWarp) >> 2;
+    const int gw = (warp - T::kFirstCvtWarp) & 3;
+    uint8_t *base = smem + pipe * T::kPipeBytes;
+    uint64_t *we = win_empty + pipe * WS, *wr = win_ready + pipe * WS;
+    constexpr int kRowsPerLane = (kWinRowsMax + 31) / 32;  // 5
+    int ws = 0;
+    uint32_t wph = 0;
+    const int howv = p.Ho * p.Wv;
+    // x has fewer than 2^31 elements on this path: 32-bit element offsets.
+    const int hw = static_cast<int>(p.HW);
+    int choff[8];  // offsets of this warp's 8 channels within a 32-channel block
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) choff[4 * h + e] = (4 * gw + 16 * h + e) * hw;
+    for (int tile = blockIdx.x + pipe * gridDim.x; tile < num_tiles; tile += P * gridDim.x) {
+      const int mb = tile / p.n_blocks;
+      const int v0 = mb * kConvBM;
+      int rbase[kRowsPerLane];  // x offset of (n, ih0, iw0) of the row
+      int rih[kRowsPerLane], riw[kRowsPerLane];
+      bool rvalid[kRowsPerLane];
+#pragma unroll
+      for (int i = 0; i < kRowsPerLane; ++i) {
+        const int r = lane + 32 * i;
+        const int v = v0 + r;
+        rvalid[i] = r < wg.win_rows && v < p.Mv;
+        int n = 0, oh = 0, ow = 0;
+        if (rvalid[i]) {
+          n = v / howv;
+          const int rem = v - n * howv;
+          oh = rem / p.Wv;
+          ow = rem - oh * p.Wv;
+        }
+        rih[i] = oh * p.sh - p.pt;
+        riw[i] = ow * p.sw - p.pl;
+        rbase[i] = n * static_cast<int>(p.CHW) + rih[i] * p.W + riw[i];
+      }
+      for (int cb = 0; cb < cblocks; ++cb) {
+        for (int kh = 0; kh < p.KH; ++kh) {
+          for (int kg = 0; kg < wg.wins_per_row; ++kg) {
+            // Load before waiting for the slot, so the load latency overlaps
+            // the MMAs still reading it.
+            float vals[kRowsPerLane][2][4];
+            const int dh = kh * p.dh, dwo = kg * p.dw;
+            const int woff = cb * kConvBK * hw + dh * p.W + dwo;
+#pragma unroll
+            for (int i = 0; i < kRowsPerLane; ++i) {
+              const int ih = rih[i] + dh, iw = riw[i] + dwo;
+              const bool ok = rvalid[i] && static_cast<unsigned>(ih) < static_cast<unsigned>(p.H) &&
+                              static_cast<unsigned>(iw) < static_cast<unsigned>(p.W);
+              const int off = rbase[i] + woff;
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  vals[i][h][e] = ok ? __ldg(p.x + (off + choff[4 * h + e])) : 0.0f;
+            }
+            if (!mbar_wait(&we[ws], wph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+              goto role_done;
+            uint8_t *slot = base + ws * T::kWinSlotBytes;
+#pragma unroll
+            for (int i = 0; i < kRowsPerLane; ++i) {
+              const int r = lane + 32 * i;
+              if (r >= wg.win_rows) continue;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t off = sw128_offset(r, gw + 4 * h);
+                float4 hi4 = make_float4(vals[i][h][0], vals[i][h][1], vals[i][h][2], vals[i][h][3]);
+                float4 lo4;
+                float t;
+                tf32_split_trunc(hi4.x, t, lo4.x);
+                tf32_split_trunc(hi4.y, t, lo4.y);
+                tf32_split_trunc(hi4.z, t, lo4.z);
+                tf32_split_trunc(hi4.w, t, lo4.w);
+                *reinterpret_cast<float4 *>(slot + off) = hi4;
+                *reinterpret_cast<float4 *>(slot + kWinBytes + off) = lo4;
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&wr[ws]);
+            if (++ws == WS) {
+              ws = 0;
+              wph ^= 1u;
+            }
+          }
+        }
+      }
+    }
   } else if (warp < T::kFirstEpiWarp) {
     // ---------------- converter warpgroup of pipeline `pipe`: lo = x - trunc(x) ----------------
     const int pipe = (warp - T::kFirstCvtWarp) >> 2;
@@ -322,6 +424,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC>::kThreads, 1)
     }
   }
 
+role_done:
   __syncthreads();
   if (warp == T::kFirstMmaWarp) {
     tc_fence_after_sync();
@@ -342,26 +445,26 @@ WinGeom win_geom(const ConvParams &p) {
   return g;
 }
 
-template <int BNC, int kAct>
+template <int BNC, int kAct, bool kGather>
 int launch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
                const ConvParams &prm, const WinGeom &wg) {
-  using T = ConvWinTraits<BNC>;
-  int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(conv_window_3xtf32_kernel<BNC, kAct>),
-                               T::kSmemBytes);
+  using T = ConvWinTraits<BNC, kGather>;
+  auto kernel = conv_window_3xtf32_kernel<BNC, kAct, kGather>;
+  int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), T::kSmemBytes);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_window_3xtf32_kernel<BNC, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(mx, mw, prm, wg);
+  kernel<<<grid, T::kThreads, T::kSmemBytes, s>>>(mx, mw, prm, wg);
   count_launch();
   return launch_result();
 }
 
-template <int BNC>
+template <int BNC, bool kGather>
 int dispatch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
                  const ConvParams &prm, const WinGeom &wg) {
-  if (prm.act == 0) return launch_win<BNC, kEpiActNone>(s, mx, mw, prm, wg);
-  if (prm.act == 1) return launch_win<BNC, kEpiActRelu>(s, mx, mw, prm, wg);
-  return launch_win<BNC, kEpiActAny>(s, mx, mw, prm, wg);
+  if (prm.act == 0) return launch_win<BNC, kEpiActNone, kGather>(s, mx, mw, prm, wg);
+  if (prm.act == 1) return launch_win<BNC, kEpiActRelu, kGather>(s, mx, mw, prm, wg);
+  return launch_win<BNC, kEpiActAny, kGather>(s, mx, mw, prm, wg);
 }
 
 }  // namespace
@@ -370,6 +473,11 @@ void conv_window_rows(const ConvParams &p, int *wv, int64_t *mv) {
   const WinGeom g = win_geom(p);
   *wv = p.Wo + (g.taps_per_win - 1) * p.dw;
   *mv = static_cast<int64_t>(p.M / p.Wo) * *wv;
+}
+
+bool conv_window_gather_supported(const ConvParams &p, int n_img) {
+  return conv_window_supported(p, n_img) &&
+         static_cast<int64_t>(n_img) * p.CHW < (int64_t(1) << 31);
 }
 
 bool conv_window_supported(const ConvParams &p, int n_img) {
@@ -393,6 +501,8 @@ bool conv_window_supported(const ConvParams &p, int n_img) {
 int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
                        const float *x_nhwc, ConvParams prm, int n_img) {
   if (!conv_window_supported(prm, n_img)) return kErrUnsupported;
+  const bool gather = x_nhwc == nullptr;  // read NCHW prm.x directly
+  if (gather && !prm.x) return kErrInvalidArg;
   const WinGeom wg = win_geom(prm);
   int wv;
   int64_t mv;
@@ -401,14 +511,23 @@ int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp,
   prm.Mv = static_cast<int>(mv);
   prm.m_blocks = static_cast<int>(ceil_div(mv, kConvBM));
   CUtensorMap mx, mw;
-  int rc = encode_tmap_im2col_nhwc_f32_sw128(
-      &mx, x_nhwc, prm.C, prm.W, prm.H, n_img, -prm.pl, -prm.pt,
-      (wv - 1) * prm.sw - prm.pl - (prm.W - 1), (prm.Ho - 1) * prm.sh - prm.pt - (prm.H - 1),
-      prm.sw, prm.sh, kConvBK, wg.win_rows);
-  if (rc) return rc;
+  int rc = kOk;
+  if (gather) {
+    mx = CUtensorMap{};  // unused
+  } else {
+    rc = encode_tmap_im2col_nhwc_f32_sw128(
+        &mx, x_nhwc, prm.C, prm.W, prm.H, n_img, -prm.pl, -prm.pt,
+        (wv - 1) * prm.sw - prm.pl - (prm.W - 1), (prm.Ho - 1) * prm.sh - prm.pt - (prm.H - 1),
+        prm.sw, prm.sh, kConvBK, wg.win_rows);
+    if (rc) return rc;
+  }
   rc = encode_tmap_2d_f32_sw128(&mw, wsplit, kp, n_blocks * 2 * bnc, kp * 4, kConvBK, 2 * bnc);
   if (rc) return rc;
-  return bnc == 64 ? dispatch_win<64>(s, mx, mw, prm, wg) : dispatch_win<128>(s, mx, mw, prm, wg);
+  if (gather)
+    return bnc == 64 ? dispatch_win<64, true>(s, mx, mw, prm, wg)
+                     : dispatch_win<128, true>(s, mx, mw, prm, wg);
+  return bnc == 64 ? dispatch_win<64, false>(s, mx, mw, prm, wg)
+                   : dispatch_win<128, false>(s, mx, mw, prm, wg);
 }
 
 }  // namespace nplk

@@ -33,6 +33,8 @@ NPL_DTYPE_FP32, NPL_DTYPE_FP16, NPL_DTYPE_BF16, NPL_DTYPE_INT8, NPL_DTYPE_INT32 
 NPL_PAD_VALID, NPL_PAD_SAME, NPL_PAD_EXPLICIT = 0, 1, 2
 NPL_POOL_MAX, NPL_POOL_AVG, NPL_POOL_GLOBAL_AVG, NPL_POOL_GLOBAL_MAX = 0, 1, 2, 3
 NPL_MAX_DIMS = 8
+NPLK_CONV_ALGO_AUTO, NPLK_CONV_ALGO_DIRECT, NPLK_CONV_ALGO_IM2COL = 0, 1, 2
+NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER = 3, 4
 NPLK_GEMM_TF32_FAST = 1
 
 
@@ -161,11 +163,14 @@ NPLK_SIGNATURES = {
                             _VP, C.c_int, _F, C.c_uint, _VP, C.c_size_t, _VP]),
     "nplk_conv_workspace_size": (C.c_size_t, [_G]),
     "nplk_conv_workspace_min_size": (C.c_size_t, [_G]),
+    "nplk_conv_workspace_size_algo": (C.c_size_t, [_G, C.c_int]),
     "nplk_conv2d_fused": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, C.c_int,
                                     _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_conv2d_prepare": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _F, _VP,
                                       C.c_size_t]),
     "nplk_conv2d_run": (C.c_int, [_VP, _G, _VP, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
+    "nplk_conv2d_run_algo": (C.c_int, [_VP, _G, _VP, C.c_int, _F, _VP, _VP, C.c_size_t, _VP,
+                                        C.c_int]),
     "nplk_conv2d_stage_input": (C.c_int, [_VP, _G, _VP, _VP, C.c_size_t]),
     "nplk_conv2d_run_staged": (C.c_int, [_VP, _G, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_conv2d_fused_noalloc": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,

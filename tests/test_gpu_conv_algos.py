@@ -1,17 +1,15 @@
-"""The TMA conv paths against the direct-gather kernel and the oracle:
-  * window path (stride_w == 1, KW > 1): input rewritten as one raw NHWC
-    plane, one im2col TMA window per (tile, channel block, kh) shared by the
-    KW taps, tf32 lo part formed in shared memory;
-  * im2col path (other strides, 1x1): NHWC tf32 hi/lo planes, one im2col TMA
-    load per k-block.
+"""Every conv kernel (nplk_conv2d_run_algo) against the direct-gather kernel
+and the oracle:
+  * IM2COL: NHWC tf32 hi/lo planes of x, one im2col TMA load per k-block;
+  * WINDOW: one raw NHWC plane, one im2col TMA window per (tile, channel
+    block, kh) shared by the KW taps (tf32 lo part formed in shared memory);
+  * WINDOW_GATHER: the same windows gathered from NCHW x by the kernel.
 
 All kernels share the k order, the split, the MMA sequence and the
-epilogue, so their outputs must agree bit for bit; the workspace size picks
-the path (nplk_conv_workspace_size: TMA path, nplk_conv_workspace_min_size:
-direct path) and the library's launch counter shows which one ran (2
-launches: NHWC rewrite + conv; 1 launch: conv). Against the oracle (the
-reference's direct conv loop) the tolerance is the 3xTF32 one: normwise max
-rel err <= 1e-4."""
+epilogue, so their outputs must agree bit for bit; the launch counter shows
+how many kernels each ran (2 for the plane-based ones: NHWC rewrite + conv).
+Against the oracle (the reference's direct conv loop) the tolerance is the
+3xTF32 one: normwise max rel err <= 1e-4."""
 import ctypes as C
 
 import numpy as np
@@ -67,7 +65,11 @@ CASES = {
 }
 
 
-def _run(lib, g, x, w, bias, bn, act, ws_bytes, work):
+ALGOS = {nb.NPLK_CONV_ALGO_DIRECT: 1, nb.NPLK_CONV_ALGO_IM2COL: 2, nb.NPLK_CONV_ALGO_WINDOW: 2,
+         nb.NPLK_CONV_ALGO_WINDOW_GATHER: 1}  # algo -> kernel launches per run
+
+
+def _run(lib, g, x, w, bias, bn, act, algo, ws_bytes, work):
     import torch
     gamma, beta, mean, var = bn
     y = torch.full((g.n, g.c_out, g.h_out, g.w_out), float("nan"), device="cuda")
@@ -77,8 +79,8 @@ def _run(lib, g, x, w, bias, bn, act, ws_bytes, work):
                                    S.dptr(work), ws_bytes) == 0
     torch.cuda.synchronize()
     lib.nplk_take_launch_count()
-    rc = lib.nplk_conv2d_run(s, C.byref(g), S.dptr(x), act, 0.01, S.dptr(y), S.dptr(work),
-                             ws_bytes, None)
+    rc = lib.nplk_conv2d_run_algo(s, C.byref(g), S.dptr(x), act, 0.01, S.dptr(y), S.dptr(work),
+                                  ws_bytes, None, algo)
     launches = lib.nplk_take_launch_count()
     assert rc == 0, rc
     torch.cuda.synchronize()
@@ -87,15 +89,21 @@ def _run(lib, g, x, w, bias, bn, act, ws_bytes, work):
 
 
 @pytest.mark.parametrize("name", list(CASES))
-def test_im2col_path_matches_direct_bitwise_and_oracle(name):
+def test_all_conv_kernels_match_direct_bitwise_and_oracle(name):
     import torch
     lib = S.gpu_lib()
     g = CASES[name]
-    full = lib.nplk_conv_workspace_size(C.byref(g))
     small = lib.nplk_conv_workspace_min_size(C.byref(g))
+    sizes = {a: lib.nplk_conv_workspace_size_algo(C.byref(g), a) for a in ALGOS}
+    assert sizes[nb.NPLK_CONV_ALGO_DIRECT] == small
     plane = g.n * g.h * g.w * g.c_in * 4
-    planes = 1 if (g.stride_w == 1 and g.kw > 1) else 2
-    assert full >= small + planes * plane, (full, small, plane)
+    if sizes[nb.NPLK_CONV_ALGO_IM2COL]:
+        assert sizes[nb.NPLK_CONV_ALGO_IM2COL] >= small + 2 * plane
+    if sizes[nb.NPLK_CONV_ALGO_WINDOW]:
+        assert sizes[nb.NPLK_CONV_ALGO_WINDOW] >= small + plane
+        assert sizes[nb.NPLK_CONV_ALGO_WINDOW_GATHER] == small
+    # every geometry here suits at least one TMA kernel
+    assert sizes[nb.NPLK_CONV_ALGO_IM2COL] or sizes[nb.NPLK_CONV_ALGO_WINDOW]
     gen = torch.Generator(device="cuda").manual_seed(len(name))
     x = torch.rand(g.n, g.c_in, g.h, g.w, device="cuda", generator=gen) * 2 - 1
     w = torch.randn(g.c_out, g.c_in, g.kh, g.kw, device="cuda", generator=gen) * 0.05
@@ -104,17 +112,34 @@ def test_im2col_path_matches_direct_bitwise_and_oracle(name):
           torch.rand(g.c_out, device="cuda", generator=gen) * 0.2 - 0.1,
           torch.randn(g.c_out, device="cuda", generator=gen) * 0.1,
           torch.rand(g.c_out, device="cuda", generator=gen) + 0.5]
-    work = torch.empty(full // 4 + 64, device="cuda")
+    work = torch.empty(max(sizes.values()) // 4 + 64, device="cuda")
     act = nb.NPL_ACT_LEAKY_RELU
-    y_tma, n_tma = _run(lib, g, x, w, bias, bn, act, full, work)
-    y_dir, n_dir = _run(lib, g, x, w, bias, bn, act, small, work)
-    assert (n_tma, n_dir) == (2, 1)
-    a, b = y_tma.cpu().numpy(), y_dir.cpu().numpy()
-    assert not np.isnan(a).any()
-    assert np.array_equal(a, b), f"max diff {np.abs(a - b).max()}"
+    outs = {}
+    for algo, n_launch in ALGOS.items():
+        if not sizes[algo]:
+            continue
+        y, launches = _run(lib, g, x, w, bias, bn, act, algo, sizes[algo], work)
+        assert launches == n_launch, (algo, launches)
+        outs[algo] = y.cpu().numpy()
+    ref_dir = outs[nb.NPLK_CONV_ALGO_DIRECT]
+    assert not np.isnan(ref_dir).any()
+    for algo, a in outs.items():
+        assert np.array_equal(a, ref_dir), f"algo {algo}: max diff {np.abs(a - ref_dir).max()}"
     ref = oracle_conv_bn(x.cpu().numpy(), w.cpu().numpy(), g, bias.cpu().numpy(),
                          [t.cpu().numpy() for t in bn], act)
-    assert S.normwise_err(a, ref) < TOL
+    assert S.normwise_err(ref_dir, ref) < TOL
+
+
+def test_algo_selection_rules():
+    lib = S.gpu_lib()
+    A = nb
+    g = geom(2, 64, 28, 28, 64, 3, 3, 1, 1, 1, 1, 1, 1)     # stride 1, 3x3: windows apply
+    assert lib.nplk_conv_workspace_size(C.byref(g)) == lib.nplk_conv_workspace_min_size(C.byref(g))
+    assert lib.nplk_conv_workspace_size_algo(C.byref(g), A.NPLK_CONV_ALGO_WINDOW_GATHER) > 0
+    g2 = geom(2, 64, 28, 28, 64, 3, 3, 2, 2, 1, 1, 1, 1)    # stride 2: im2col planes
+    assert lib.nplk_conv_workspace_size(C.byref(g2)) == \
+        lib.nplk_conv_workspace_size_algo(C.byref(g2), A.NPLK_CONV_ALGO_IM2COL)
+    assert lib.nplk_conv_workspace_size_algo(C.byref(g2), 99) == 0
 
 
 def test_small_or_unaligned_geometries_keep_the_direct_path():
@@ -124,3 +149,6 @@ def test_small_or_unaligned_geometries_keep_the_direct_path():
               geom(1, 32, 64, 64, 32, 9, 9, 9, 9, 0, 0, 1, 1)):     # stride above 8
         assert lib.nplk_conv_workspace_size(C.byref(g)) == \
             lib.nplk_conv_workspace_min_size(C.byref(g))
+        for algo in (nb.NPLK_CONV_ALGO_IM2COL, nb.NPLK_CONV_ALGO_WINDOW,
+                     nb.NPLK_CONV_ALGO_WINDOW_GATHER):
+            assert lib.nplk_conv_workspace_size_algo(C.byref(g), algo) == 0
