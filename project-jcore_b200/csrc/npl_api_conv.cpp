@@ -78,6 +78,114 @@ bool all_fp32(const npl_tensor_t *a, const npl_tensor_t *b, const npl_tensor_t *
          c->dtype == NPL_DTYPE_FP32 && (!d || d->dtype == NPL_DTYPE_FP32);
 }
 
+// Inference-mode conv on page-locked host input and output: the batch is cut
+// into chunks whose host-to-device copy, conv and device-to-host copy run on
+// three streams, so the PCIe transfers in both directions overlap each
+// other and the kernels (a synchronous whole-batch call would copy in,
+// compute and copy out one after the other). The first and last chunks are
+// small (1/16 of the batch), which shortens the copy-in before the first
+// conv and the copy-out after the last; the middle ones take about a quarter
+// of the batch each. Same kernels and per-image results as the unchunked
+// call.
+constexpr size_t kPipelineMinBytes = size_t(8) << 20;
+constexpr int kPipelineMaxChunks = 8;
+
+// Chunk sizes (images) for a batch of n >= 2: {e, m, ..., m', e}.
+int pipeline_chunks(int n, int *sizes) {
+  const int e = n / 16 > 0 ? n / 16 : 1;
+  int rest = n - 2 * e;
+  int k = 0;
+  sizes[k++] = e;
+  if (rest > 0) {
+    const int mid = (rest + 3) / 4;  // at most four middle chunks
+    while (rest > 0) {
+      const int c = rest < mid ? rest : mid;
+      sizes[k++] = c;
+      rest -= c;
+    }
+  }
+  sizes[k++] = e;
+  return k;
+}
+
+int run_conv_pipelined(const nplk_conv_geom_t &g, const npl_tensor_t *input,
+                       const npl_tensor_t *weights, const npl_tensor_t *bias,
+                       const npl_batchnorm_params_t *bn, int act, float act_alpha,
+                       npl_tensor_t *output, npl_perf_stats_t *stats, const char *backend) {
+  const size_t co = static_cast<size_t>(g.c_out);
+  const size_t in_img = static_cast<size_t>(g.c_in * g.h * g.w);
+  const size_t out_img = static_cast<size_t>(g.c_out * g.h_out * g.w_out);
+  const size_t w_elems = static_cast<size_t>(g.c_out * g.c_in * g.kh * g.kw);
+  const int n = static_cast<int>(g.n);
+  int sizes[kPipelineMaxChunks];
+  const int chunks = pipeline_chunks(n, sizes);
+  int per = 0;
+  for (int c = 0; c < chunks; ++c) per = sizes[c] > per ? sizes[c] : per;
+  npl::CopyLanes *lanes = npl::copy_lanes(2 * static_cast<size_t>(chunks) + 2);
+  if (!lanes) return NPL_ERR_INTERNAL;
+  npl::Call call;
+  const float *w = call.input(weights->data, w_elems * 4);
+  const float *b = bias ? call.input(bias->data, co * 4) : nullptr;
+  const float *mean = nullptr, *var = nullptr, *gamma = nullptr, *beta = nullptr;
+  if (bn) {
+    mean = call.param(bn->mean, co);
+    var = call.param(bn->variance, co);
+    gamma = call.param(bn->gamma, co);
+    beta = call.param(bn->beta, co);
+  }
+  nplk_conv_geom_t gc = g;
+  gc.n = per;
+  const size_t ws = nplk_conv_workspace_size(&gc);
+  void *work = call.scratch(ws);
+  float *dx = static_cast<float *>(call.scratch(in_img * n * 4));
+  float *dy = static_cast<float *>(call.scratch(out_img * n * 4));
+  if (call.status()) return call.finish(nullptr, 0, 0, nullptr);
+  cudaStream_t s = call.stream();
+  cudaEvent_t *ev = lanes->events.data();  // [0]: buffers ready, [1]: copies out done
+  cudaEvent_t *ev_in = ev + 2, *ev_done = ev + 2 + chunks;
+  const float *hx = static_cast<const float *>(input->data);
+  float *hy = static_cast<float *>(output->data);
+  call.start_timer();
+  call.fail(nplk_conv2d_prepare(s, &gc, w, b, mean, var, gamma, beta, bn ? bn->epsilon : 0.0f,
+                                work, ws));
+  auto ok = [&](cudaError_t e) {
+    if (e != cudaSuccess) call.fail(NPL_ERR_INTERNAL);
+    return e == cudaSuccess;
+  };
+  if (!call.status() && ok(cudaEventRecord(ev[0], s)) &&
+      ok(cudaStreamWaitEvent(lanes->in, ev[0], 0)) && ok(cudaStreamWaitEvent(lanes->out, ev[0], 0))) {
+    int i0 = 0;
+    for (int c = 0; c < chunks && !call.status(); i0 += sizes[c], ++c) {
+      const int nc = sizes[c];
+      gc.n = nc;
+      const size_t xo = static_cast<size_t>(i0) * in_img, yo = static_cast<size_t>(i0) * out_img;
+      if (!ok(cudaMemcpyAsync(dx + xo, hx + xo, nc * in_img * 4, cudaMemcpyHostToDevice,
+                              lanes->in)) ||
+          !ok(cudaEventRecord(ev_in[c], lanes->in)) || !ok(cudaStreamWaitEvent(s, ev_in[c], 0)))
+        break;
+      call.fail(nplk_conv2d_run(s, &gc, dx + xo, act, act_alpha, dy + yo, work, ws, nullptr));
+      if (call.status() || !ok(cudaEventRecord(ev_done[c], s)) ||
+          !ok(cudaStreamWaitEvent(lanes->out, ev_done[c], 0)) ||
+          !ok(cudaMemcpyAsync(hy + yo, dy + yo, nc * out_img * 4, cudaMemcpyDeviceToHost,
+                              lanes->out)))
+        break;
+    }
+  }
+  // Everything below on the call's stream (frees, status read) waits for the
+  // last copies, also after an error.
+  if (cudaEventRecord(ev[1], lanes->out) != cudaSuccess || cudaStreamWaitEvent(s, ev[1], 0) != cudaSuccess) {
+    cudaStreamSynchronize(lanes->out);
+    cudaStreamSynchronize(lanes->in);
+    call.fail(NPL_ERR_INTERNAL);
+  }
+  cudaEventRecord(ev[0], lanes->in);
+  cudaStreamWaitEvent(s, ev[0], 0);
+  call.stop_timer();
+  const double flops = 2.0 * g.n * g.c_out * g.c_in * g.h_out * g.w_out * g.kh * g.kw;
+  const int fused = 1 + (bn ? 1 : 0) + (act != NPLK_ACT_NONE ? 1 : 0);
+  return call.finish(stats, flops, 4.0 * (in_img * n + w_elems + out_img * n), backend, fused);
+}
+
 // Runs conv (+bias) (+BN) (+act) through the implicit-GEMM kernel.
 int run_conv(const npl_tensor_t *input, const npl_tensor_t *weights, const npl_tensor_t *bias,
              const npl_conv_params_t *params, const npl_batchnorm_params_t *bn, int act,
@@ -98,6 +206,11 @@ int run_conv(const npl_tensor_t *input, const npl_tensor_t *weights, const npl_t
   }
   const size_t co = static_cast<size_t>(g.c_out);
   const bool train_bn = bn && bn->training;
+  if (!train_bn && g.n >= 2 && in_elems * 4 >= kPipelineMinBytes &&
+      npl::is_pinned_host(input->data) && npl::is_pinned_host(output->data) &&
+      input->data != output->data)
+    return run_conv_pipelined(g, input, weights, bias, bn, act, act_alpha, output, stats,
+                              backend);
   npl::Call call;
   const float *x = call.input(input->data, in_elems * 4);
   const float *w = call.input(weights->data, w_elems * 4);

@@ -73,7 +73,60 @@ int map_err(cudaError_t e) {
   return NPL_ERR_INTERNAL;
 }
 
+// Kept for the thread's lifetime (no destructor: CUDA may already be shut
+// down when thread-local objects die at process exit).
+struct ThreadLanes {
+  int device = -1;
+  CopyLanes lanes;
+  void release() {
+    if (device < 0) return;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    for (cudaEvent_t e : lanes.events) cudaEventDestroy(e);
+    if (lanes.in) cudaStreamDestroy(lanes.in);
+    if (lanes.out) cudaStreamDestroy(lanes.out);
+    cudaSetDevice(cur);
+    lanes = CopyLanes{};
+    device = -1;
+  }
+};
+thread_local ThreadLanes t_lanes;
+
 }  // namespace
+
+CopyLanes *copy_lanes(size_t events) {
+  const int dev = state().device;
+  if (t_lanes.device != dev) {
+    t_lanes.release();
+    if (cudaStreamCreateWithFlags(&t_lanes.lanes.in, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&t_lanes.lanes.out, cudaStreamNonBlocking) != cudaSuccess) {
+      cudaGetLastError();
+      t_lanes.device = dev;
+      t_lanes.release();
+      return nullptr;
+    }
+    t_lanes.device = dev;
+  }
+  while (t_lanes.lanes.events.size() < events) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    t_lanes.lanes.events.push_back(e);
+  }
+  return &t_lanes.lanes;
+}
+
+bool is_pinned_host(const void *p) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost;
+}
 
 Call::Call() {
   State &s = state();

@@ -96,6 +96,19 @@ class Call {
   bool timed_ = false;
 };
 
+// Copy/compute overlap within one call: two auxiliary non-blocking streams
+// (host-to-device and device-to-host copies) and a pool of events without
+// timing, created once per thread for the library's device.
+struct CopyLanes {
+  cudaStream_t in = nullptr;
+  cudaStream_t out = nullptr;
+  std::vector<cudaEvent_t> events;
+};
+// The calling thread's lanes with at least `events` events, or NULL on error.
+CopyLanes *copy_lanes(size_t events);
+// True for page-locked host memory (asynchronous copies overlap compute).
+bool is_pinned_host(const void *p);
+
 // Reference-compatible helpers shared by several operators.
 int validate_conv_params(const npl_conv_params_t *p);
 

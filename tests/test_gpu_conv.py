@@ -209,3 +209,37 @@ def test_conv_device_pointers_and_stats():
     xn, wn = x.cpu().numpy(), w.cpu().numpy()
     ref = S.o_activation(S.o_conv2d(xn, wn, pad=(1, 1)), 1)
     assert S.normwise_err(y.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("n", [16, 13])
+def test_conv_bn_act_pinned_host_buffers_pipelined(n):
+    # Page-locked host input/output take the chunked copy/compute pipeline
+    # (n = 13: the last chunk is ragged); per-image results are those of the
+    # same call on device tensors, bit for bit.
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator().manual_seed(n)
+    x = torch.rand(n, 64, 56, 56, generator=gen).pin_memory()
+    w = (torch.randn(64, 64, 3, 3, generator=gen) * 0.05).pin_memory()
+    bn = [(torch.rand(64, generator=gen) + 0.5) for _ in range(4)]
+    y = torch.zeros(n, 64, 56, 56).pin_memory()
+    p = nb.conv_params(3, 3, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    bnp = nb.NplBatchnormParams(bn[0].data_ptr(), bn[1].data_ptr(), bn[2].data_ptr(),
+                                bn[3].data_ptr(), 1e-5, 0, 0.1)
+    t = lambda a: nb.tensor(lib, a.data_ptr(), a.shape)  # noqa: E731
+    st = nb.NplPerfStats()
+    rc = lib.npl_conv2d_bn_activation(C.byref(t(x)), C.byref(t(w)), None, C.byref(p),
+                                      C.byref(bnp), nb.NPL_ACT_RELU, C.byref(t(y)), C.byref(st))
+    assert rc == 0
+    assert st.was_fused == 1 and st.elapsed_ms > 0
+    xd, wd, yd = x.cuda(), w.cuda(), torch.zeros(n, 64, 56, 56, device="cuda")
+    bnd = [v.cuda() for v in bn]
+    bnpd = nb.NplBatchnormParams(*(v.data_ptr() for v in bnd), 1e-5, 0, 0.1)
+    rc = lib.npl_conv2d_bn_activation(C.byref(t(xd)), C.byref(t(wd)), None, C.byref(p),
+                                      C.byref(bnpd), nb.NPL_ACT_RELU, C.byref(t(yd)), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y, yd.cpu())
+    mean, var, gamma, beta = (b.numpy() for b in bn)
+    ref = oracle_fused(x[:2].numpy(), w.numpy(), (gamma, beta, mean, var), 1, pad=(1, 1))
+    assert S.normwise_err(y[:2].numpy(), ref) < TOL
