@@ -2,7 +2,10 @@
 ``ncu``). Each case allocates its inputs on cuda:0, runs the kernel a few times
 and checks the kernel status word.
 
-    python -m npl_b200.profile_cases conv      # 3x3 conv+BN+ReLU, N=32 64->64 56x56
+    python -m npl_b200.profile_cases conv      # 3x3 conv+BN+ReLU, N=32 64->64 56x56 (default kernel)
+    python -m npl_b200.profile_cases conv_direct  # the same on the direct-gather kernel
+    python -m npl_b200.profile_cases conv_window_tma  # ... on TMA windows over an NHWC plane
+    python -m npl_b200.profile_cases conv_s2   # 3x3 stride 2, N=32 64->128 56x56 (im2col kernel)
     python -m npl_b200.profile_cases stem      # 7x7/s2 conv+BN+ReLU, N=16 3->64 224x224
     python -m npl_b200.profile_cases gemm      # 4096x4096x8192 3xTF32 GEMM
     python -m npl_b200.profile_cases chain     # depthwise, BN, ReLU, GAP, softmax 256x512x14x14
@@ -29,7 +32,7 @@ def _p(t):
 
 
 def case_conv(reps: int = 3, n: int = 32, c: int = 64, hw: int = 56, cout: int = 64,
-              k: int = 3, stride: int = 1, pad: int = 1):
+              k: int = 3, stride: int = 1, pad: int = 1, algo: int = 0):
     from . import conv_geom
     torch, lib, s = _setup()
     gen = torch.Generator(device="cuda").manual_seed(0)
@@ -38,11 +41,15 @@ def case_conv(reps: int = 3, n: int = 32, c: int = 64, hw: int = 56, cout: int =
     bn = [torch.rand(cout, device="cuda", generator=gen) + 0.5 for _ in range(4)]
     g = conv_geom(n, c, hw, hw, cout, k, k, stride, pad)
     y = torch.empty(n, cout, g.h_out, g.w_out, device="cuda")
-    ws = lib.nplk_conv_workspace_size(C.byref(g))
+    ws = lib.nplk_conv_workspace_size_algo(C.byref(g), algo)
+    assert ws > 0
     work = torch.empty(ws // 4 + 64, device="cuda")
     for _ in range(reps):
-        rc = lib.nplk_conv2d_fused(s, C.byref(g), _p(x), _p(w), None, _p(bn[0]), _p(bn[1]),
-                                   _p(bn[2]), _p(bn[3]), 1e-5, 1, 0.0, _p(y), _p(work), ws, None)
+        rc = lib.nplk_conv2d_prepare(s, C.byref(g), _p(w), None, _p(bn[0]), _p(bn[1]), _p(bn[2]),
+                                     _p(bn[3]), 1e-5, _p(work), ws)
+        assert rc == 0, rc
+        rc = lib.nplk_conv2d_run_algo(s, C.byref(g), _p(x), 1, 0.0, _p(y), _p(work), ws, None,
+                                      algo)
         assert rc == 0, rc
     torch.cuda.synchronize()
     assert lib.nplk_read_status(s) == 0
@@ -99,7 +106,11 @@ def case_layernorm(reps: int = 3):
     torch.cuda.synchronize()
 
 
-CASES = {"conv": case_conv, "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
+CASES = {"conv": case_conv,
+         "conv_direct": lambda: case_conv(algo=1),
+         "conv_window_tma": lambda: case_conv(algo=3),
+         "conv_s2": lambda: case_conv(cout=128, stride=2),
+         "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
          "layernorm": case_layernorm}
 
 if __name__ == "__main__":
