@@ -39,19 +39,25 @@ constexpr int kWinMaxExtra = 8;                                   // (KW-1)*dw l
 constexpr int kWinRowsMax = kConvBM + kWinMaxExtra;               // 136
 constexpr int kWinBytes = kWinRowsMax * kConvBK * 4;              // 17 KB, 1024-aligned
 
+// Shared memory: per pipeline kWinSlots window slots (x and lo parts), then
+// one ring of weight slabs that all pipelines read. With two pipelines
+// (C_out <= 64, a single output-channel block) every tile walks the same
+// slab sequence, so both MMA warps consume each slab (one TMA load serves
+// both, and the ring is twice as deep as two private rings in the same
+// space).
 template <int BNC, bool kGather>
 struct ConvWinTraits {
   static constexpr int kPipes = BNC == 64 ? 2 : 1;
   static constexpr int kWinSlots = BNC == 64 ? 2 : 3;  // per pipeline
-  static constexpr int kBSlots = BNC == 64 ? 2 : 3;    // per pipeline
+  static constexpr int kBSlots = BNC == 64 ? 4 : 3;    // shared
   static constexpr int kBBytes = 2 * BNC * kConvBK * 4;
-  static constexpr int kWinSlotBytes = 2 * kWinBytes;  // raw + lo
-  static constexpr int kPipeBytes = kWinSlots * kWinSlotBytes + kBSlots * kBBytes;
-  // warps [0, kProdWarps): TMA producers, per pipeline one for the weight
-  // slabs and (TMA windows only) one for the windows; then one MMA warp per
-  // pipeline, 4 window warps per pipeline (converter or gather), 4 epilogue
-  // warps.
-  static constexpr int kProdWarps = kGather ? kPipes : 2 * kPipes;
+  static constexpr int kWinSlotBytes = 2 * kWinBytes;  // x + lo
+  static constexpr int kWinAreaBytes = kPipes * kWinSlots * kWinSlotBytes;
+  static constexpr int kPipeBytes = kWinAreaBytes + kBSlots * kBBytes;  // all stage memory
+  // warp 0: weight-slab producer; warps 1..kPipes (TMA windows only): window
+  // producers; then one MMA warp per pipeline, 4 window warps per pipeline
+  // (converter or gather), 4 epilogue warps.
+  static constexpr int kProdWarps = kGather ? 1 : 1 + kPipes;
   static constexpr int kFirstMmaWarp = kProdWarps;
   static constexpr int kFirstCvtWarp = kProdWarps + kPipes;
   static constexpr int kFirstEpiWarp = kFirstCvtWarp + 4 * kPipes;
@@ -60,7 +66,7 @@ struct ConvWinTraits {
   static constexpr int kAccPerPipe = 2;
   static constexpr int kTmemCols = kPipes * kAccPerPipe * kAccCols;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kPipes * kPipeBytes + kBarrierBytes + BNC * 20;
+  static constexpr int kSmemBytes = 1024 + kPipeBytes + kBarrierBytes + BNC * 20;
   static_assert(kTmemCols == 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -87,13 +93,14 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
-  uint8_t *bars = smem + P * T::kPipeBytes;
+  uint8_t *bslots = smem + T::kWinAreaBytes;
+  uint8_t *bars = smem + T::kPipeBytes;
   uint64_t *win_full = reinterpret_cast<uint64_t *>(bars);  // [P][WS] raw window landed
   uint64_t *win_ready = win_full + P * WS;                   // [P][WS] lo part written
   uint64_t *win_empty = win_ready + P * WS;                  // [P][WS] MMAs done with it
-  uint64_t *b_full = win_empty + P * WS;                     // [P][BS]
-  uint64_t *b_empty = b_full + P * BS;                       // [P][BS]
-  uint64_t *acc_full = b_empty + P * BS;                     // [P * kAccPerPipe]
+  uint64_t *b_full = win_empty + P * WS;                     // [BS]
+  uint64_t *b_empty = b_full + BS;                           // [BS], one arrival per pipeline
+  uint64_t *acc_full = b_empty + BS;                         // [P * kAccPerPipe]
   uint64_t *acc_empty = acc_full + P * T::kAccPerPipe;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + P * T::kAccPerPipe);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -109,9 +116,9 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
       mbar_init(&win_ready[s], 4);
       mbar_init(&win_empty[s], 1);
     }
-    for (int s = 0; s < P * BS; ++s) {
+    for (int s = 0; s < BS; ++s) {
       mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
+      mbar_init(&b_empty[s], P);
     }
     for (int a = 0; a < P * T::kAccPerPipe; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -137,24 +144,54 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   // runs it. Per tile: windows (cb, kh, kw group) in that order, each
   // followed by its taps_per_win weight slabs.
 
-  if (warp < T::kProdWarps) {
-    // ---------------- TMA producers of pipeline `pipe` ----------------
-    // Windows and weight slabs come from two threads, so that a window can
-    // be requested as soon as its slot is free (a whole window of MMA work
-    // ahead), not only after the previous window's slabs were issued.
-    const int pipe = kGather ? warp : warp >> 1;
-    const bool slabs = kGather || (warp & 1) != 0;
+  if (warp == 0) {
+    // ---------------- weight-slab producer (all pipelines) ----------------
+    // Round r carries the slabs of each pipeline's r-th tile; with two
+    // pipelines those tiles share one output-channel block, so one sequence
+    // serves both. A pipeline without an r-th tile is stood in for by an
+    // extra arrival on the slab's empty barrier.
     if (lane == 0) {
-      uint8_t *base = smem + pipe * T::kPipeBytes;
-      uint8_t *bslots = base + WS * T::kWinSlotBytes;
+      int bs = 0;
+      uint32_t bph = 0;
+      uint32_t b_issued = 0, b_issued_ph = 0;
+      for (int r = 0;; ++r) {
+        const int tile = blockIdx.x + P * r * gridDim.x;  // pipeline 0's r-th tile
+        if (tile >= num_tiles) break;
+        int missing = 0;
+        for (int q = 1; q < P; ++q)
+          if (tile + q * static_cast<int>(gridDim.x) >= num_tiles) ++missing;
+        const int nb = tile - (tile / p.n_blocks) * p.n_blocks;  // 0 when P > 1
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&b_empty[bs], bph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+            goto producer_done;
+          mbar_arrive_expect_tx(&b_full[bs], T::kBBytes);
+          tma_load_2d(&map_w, &b_full[bs], bslots + bs * T::kBBytes, kb * kConvBK, nb * 2 * BNC);
+          for (int q = 0; q < missing; ++q) mbar_arrive(&b_empty[bs]);
+          b_issued |= 1u << bs;
+          b_issued_ph = (b_issued_ph & ~(1u << bs)) | (bph << bs);
+          if (++bs == BS) {
+            bs = 0;
+            bph ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // Let every issued copy land before the CTA can exit (all of them
+      // already have unless the CTA aborted).
+      for (int s = 0; s < BS; ++s)
+        if (b_issued & (1u << s)) mbar_drain(&b_full[s], (b_issued_ph >> s) & 1u);
+    }
+  } else if (warp < T::kProdWarps) {
+    // ---------------- window TMA producer of pipeline `pipe` (raw NHWC plane) ----------------
+    const int pipe = warp - 1;
+    if (lane == 0) {
+      uint8_t *wbase = smem + pipe * WS * T::kWinSlotBytes;
       uint64_t *wf = win_full + pipe * WS, *we = win_empty + pipe * WS;
-      uint64_t *bf = b_full + pipe * BS, *be = b_empty + pipe * BS;
-      int ws = 0, bs = 0;
-      uint32_t wph = 0, bph = 0;
-      uint32_t w_issued = 0, w_issued_ph = 0, b_issued = 0, b_issued_ph = 0;
+      int ws = 0;
+      uint32_t wph = 0;
+      uint32_t w_issued = 0, w_issued_ph = 0;
       for (int tile = blockIdx.x + pipe * gridDim.x; tile < num_tiles; tile += P * gridDim.x) {
         const int mb = tile / p.n_blocks;
-        const int nb = tile - mb * p.n_blocks;
         const int v0 = mb * kConvBM;
         const int howv = p.Ho * p.Wv;
         const int n0 = v0 / howv;
@@ -166,46 +203,25 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
         for (int cb = 0; cb < cblocks; ++cb) {
           for (int kh = 0; kh < p.KH; ++kh) {
             for (int kg = 0; kg < wg.wins_per_row; ++kg) {
-              if (!slabs) {
-                if (!mbar_wait(&we[ws], wph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
-                  goto producer_done;
-                mbar_arrive_expect_tx(&wf[ws], win_bytes);
-                tma_load_im2col_4d(&map_x, &wf[ws], base + ws * T::kWinSlotBytes, cb * kConvBK,
-                                   w0, h0, n0, static_cast<uint16_t>(kg * p.dw),
-                                   static_cast<uint16_t>(kh * p.dh));
-                w_issued |= 1u << ws;
-                w_issued_ph = (w_issued_ph & ~(1u << ws)) | (wph << ws);
-                if (++ws == WS) {
-                  ws = 0;
-                  wph ^= 1u;
-                }
-                continue;
-              }
-              for (int t = 0; t < wg.taps_per_win; ++t) {
-                const int kb = (cb * p.KH + kh) * p.KW + kg * wg.taps_per_win + t;
-                if (!mbar_wait(&be[bs], bph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
-                  goto producer_done;
-                mbar_arrive_expect_tx(&bf[bs], T::kBBytes);
-                tma_load_2d(&map_w, &bf[bs], bslots + bs * T::kBBytes, kb * kConvBK,
-                            nb * 2 * BNC);
-                b_issued |= 1u << bs;
-                b_issued_ph = (b_issued_ph & ~(1u << bs)) | (bph << bs);
-                if (++bs == BS) {
-                  bs = 0;
-                  bph ^= 1u;
-                }
+              if (!mbar_wait(&we[ws], wph ^ 1u, abort_flag, p.status, kStatusTimeoutProducer))
+                goto window_done;
+              mbar_arrive_expect_tx(&wf[ws], win_bytes);
+              tma_load_im2col_4d(&map_x, &wf[ws], wbase + ws * T::kWinSlotBytes, cb * kConvBK, w0,
+                                 h0, n0, static_cast<uint16_t>(kg * p.dw),
+                                 static_cast<uint16_t>(kh * p.dh));
+              w_issued |= 1u << ws;
+              w_issued_ph = (w_issued_ph & ~(1u << ws)) | (wph << ws);
+              if (++ws == WS) {
+                ws = 0;
+                wph ^= 1u;
               }
             }
           }
         }
       }
-    producer_done:
-      // Let every issued copy land before the CTA can exit (all of them
-      // already have unless the CTA aborted).
+    window_done:
       for (int s = 0; s < WS; ++s)
         if (w_issued & (1u << s)) mbar_drain(&wf[s], (w_issued_ph >> s) & 1u);
-      for (int s = 0; s < BS; ++s)
-        if (b_issued & (1u << s)) mbar_drain(&bf[s], (b_issued_ph >> s) & 1u);
     }
   } else if (warp < T::kFirstCvtWarp) {
     // ---------------- MMA issuer of pipeline `pipe` ----------------
@@ -213,12 +229,11 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_2n = umma_idesc_tf32(kConvBM, 2 * BNC);
       const uint32_t idesc_n = umma_idesc_tf32(kConvBM, BNC);
-      uint8_t *base = smem + pipe * T::kPipeBytes;
-      const uint64_t win_desc0 = umma_desc_sw128(smem_u32(base));
-      const uint64_t b_desc0 = umma_desc_sw128(smem_u32(base + WS * T::kWinSlotBytes));
+      const uint64_t win_desc0 = umma_desc_sw128(smem_u32(smem + pipe * WS * T::kWinSlotBytes));
+      const uint64_t b_desc0 = umma_desc_sw128(smem_u32(bslots));
       constexpr uint64_t kLoOff = kWinBytes >> 4;
       uint64_t *wr = win_ready + pipe * WS, *we = win_empty + pipe * WS;
-      uint64_t *bf = b_full + pipe * BS, *be = b_empty + pipe * BS;
+      uint64_t *bf = b_full, *be = b_empty;
       int ws = 0, bs = 0;
       uint32_t wph = 0, bph = 0;
       int jj = 0;
@@ -277,7 +292,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     // pixels, so each load instruction reads consecutive input columns).
     const int pipe = (warp - T::kFirstCvtWarp) >> 2;
     const int gw = (warp - T::kFirstCvtWarp) & 3;
-    uint8_t *base = smem + pipe * T::kPipeBytes;
+    uint8_t *base = smem + pipe * WS * T::kWinSlotBytes;
     uint64_t *we = win_empty + pipe * WS, *wr = win_ready + pipe * WS;
     constexpr int kRowsPerLane = (kWinRowsMax + 31) / 32;  // 5
     int ws = 0;
@@ -368,7 +383,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     // ---------------- converter warpgroup of pipeline `pipe`: lo = x - trunc(x) ----------------
     const int pipe = (warp - T::kFirstCvtWarp) >> 2;
     const int ct = threadIdx.x - (T::kFirstCvtWarp + pipe * 4) * 32;  // 0..127
-    uint8_t *base = smem + pipe * T::kPipeBytes;
+    uint8_t *base = smem + pipe * WS * T::kWinSlotBytes;
     uint64_t *wf = win_full + pipe * WS, *wr = win_ready + pipe * WS;
     const int chunks = win_bytes >> 4;  // 16-byte chunks of the window
     int ws = 0;
@@ -502,6 +517,7 @@ int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp,
                        const float *x_nhwc, ConvParams prm, int n_img) {
   if (!conv_window_supported(prm, n_img)) return kErrUnsupported;
   const bool gather = x_nhwc == nullptr;  // read NCHW prm.x directly
+  if (bnc == 64 && n_blocks != 1) return kErrUnsupported;  // pipelines share one slab sequence
   if (gather && !prm.x) return kErrInvalidArg;
   const WinGeom wg = win_geom(prm);
   int wv;
