@@ -143,10 +143,12 @@ bool conv_im2col_supported(const ConvParams &prm, int n_img);
 int launch_nchw_to_nhwc_split(cudaStream_t s, const float *x, float *hi, float *lo, int n,
                               int c, int64_t hw);
 
-// Window conv (conv_window.cu) over the raw NHWC plane x_nhwc; its GEMM rows
-// are the virtual pixels given by conv_window_rows.
+// Window conv (conv_window.cu) over the raw NHWC plane x_nhwc, or gathering
+// from NCHW prm.x when x_nhwc is NULL; its GEMM rows are the virtual pixels
+// given by conv_window_rows. after_prep: the previous kernel in the stream
+// is this call's conv_prep_kernel (the gather form then overlaps it).
 int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
-                       const float *x_nhwc, ConvParams prm, int n_img);
+                       const float *x_nhwc, ConvParams prm, int n_img, bool after_prep = false);
 bool conv_window_supported(const ConvParams &prm, int n_img);
 // The gather variant also needs x to have fewer than 2^31 elements.
 bool conv_window_gather_supported(const ConvParams &prm, int n_img);

@@ -360,6 +360,9 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
     ep[kEpBeta * cout_pad + c] = (in && beta) ? beta[c] : 0.0f;
     ep[kEpInvStd * cout_pad + c] = (in && var) ? 1.0f / sqrtf(var[c] + eps) : 1.0f;
   }
+  // The conv kernel that follows in nplk_conv2d_fused may start now; it
+  // waits (griddep_wait) before reading what this kernel wrote.
+  griddep_launch_dependents();
 }
 
 namespace {
@@ -610,14 +613,16 @@ bool has_planes(const ConvPlan &c, size_t workspace_bytes) {
 namespace {
 
 // Runs plan `c` (workspace already checked against c.full_bytes()).
+// after_prep: the previous kernel in the stream is this call's
+// conv_prep_kernel (nplk_conv2d_fused), which the gather kernel may overlap.
 int run_plan(cudaStream_t s, const nplk_conv_geom_t *g, const float *x, const ConvPlan &c,
-             ConvParams prm, void *workspace, bool stage) {
+             ConvParams prm, void *workspace, bool stage, bool after_prep = false) {
   const float *wsplit = static_cast<const float *>(workspace);
   const int n = static_cast<int>(g->n);
   switch (c.path) {
     case kPathWindowGather:
       prm.x = x;
-      return launch_conv_window(s, c.bnc, wsplit, c.kp, c.n_blocks, nullptr, prm, n);
+      return launch_conv_window(s, c.bnc, wsplit, c.kp, c.n_blocks, nullptr, prm, n, after_prep);
     case kPathWindow:
     case kPathIm2col: {
       if (stage) {
@@ -665,9 +670,10 @@ extern "C" int nplk_conv2d_run_staged(void *stream, const nplk_conv_geom_t *g, i
   return run_plan(static_cast<cudaStream_t>(stream), g, nullptr, c, prm, workspace, false);
 }
 
-extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
-                               int act, float act_alpha, float *out, void *workspace,
-                               size_t workspace_bytes, int *status) {
+namespace {
+
+int run_auto(void *stream, const nplk_conv_geom_t *g, const float *x, int act, float act_alpha,
+             float *out, void *workspace, size_t workspace_bytes, int *status, bool after_prep) {
   ConvPlan c;
   ConvParams prm;
   int rc = begin_run(g, workspace, workspace_bytes, act, act_alpha, out, status, &c, &prm);
@@ -676,7 +682,15 @@ extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const fl
   // A workspace too small for the planes of the chosen kernel selects the
   // direct kernel (same results).
   if (workspace_bytes < c.full_bytes()) c.path = kPathDirect;
-  return run_plan(static_cast<cudaStream_t>(stream), g, x, c, prm, workspace, true);
+  return run_plan(static_cast<cudaStream_t>(stream), g, x, c, prm, workspace, true, after_prep);
+}
+
+}  // namespace
+
+extern "C" int nplk_conv2d_run(void *stream, const nplk_conv_geom_t *g, const float *x,
+                               int act, float act_alpha, float *out, void *workspace,
+                               size_t workspace_bytes, int *status) {
+  return run_auto(stream, g, x, act, act_alpha, out, workspace, workspace_bytes, status, false);
 }
 
 extern "C" int nplk_conv2d_run_algo(void *stream, const nplk_conv_geom_t *g, const float *x,
@@ -703,5 +717,5 @@ extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const 
   int rc = nplk_conv2d_prepare(stream, g, w, bias, bn_mean, bn_var, bn_gamma, bn_beta, bn_eps,
                                workspace, workspace_bytes);
   if (rc) return rc;
-  return nplk_conv2d_run(stream, g, x, act, act_alpha, out, workspace, workspace_bytes, status);
+  return run_auto(stream, g, x, act, act_alpha, out, workspace, workspace_bytes, status, true);
 }

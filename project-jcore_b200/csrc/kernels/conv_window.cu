@@ -151,6 +151,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     // serves both. A pipeline without an r-th tile is stood in for by an
     // extra arrival on the slab's empty barrier.
     if (lane == 0) {
+      griddep_wait();  // the slabs may come from the weight preparation just before
       int bs = 0;
       uint32_t bph = 0;
       uint32_t b_issued = 0, b_issued_ph = 0;
@@ -422,6 +423,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     // ---------------- epilogue (4 warps, one per TMEM lane quadrant) ----------------
     const int quad = warp & 3;
     const int et = threadIdx.x - T::kFirstEpiWarp * 32;  // 0..127
+    griddep_wait();  // the epilogue constants, likewise
     int j = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++j) {
       const int pipe = j % P;
@@ -462,13 +464,31 @@ WinGeom win_geom(const ConvParams &p) {
 
 template <int BNC, int kAct, bool kGather>
 int launch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
-               const ConvParams &prm, const WinGeom &wg) {
+               const ConvParams &prm, const WinGeom &wg, bool after_prep) {
   using T = ConvWinTraits<BNC, kGather>;
   auto kernel = conv_window_3xtf32_kernel<BNC, kAct, kGather>;
   int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), T::kSmemBytes);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  if (after_prep) {
+    // Overlap with the weight preparation launched just before: the gather
+    // warps only read x (complete before the preparation started); the slab
+    // producer and the epilogue wait for the preparation's writes.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(T::kThreads);
+    cfg.dynamicSmemBytes = T::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mx, mw, prm, wg);
+    count_launch();
+    return map_cuda_error(e);
+  }
   kernel<<<grid, T::kThreads, T::kSmemBytes, s>>>(mx, mw, prm, wg);
   count_launch();
   return launch_result();
@@ -476,10 +496,10 @@ int launch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
 
 template <int BNC, bool kGather>
 int dispatch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
-                 const ConvParams &prm, const WinGeom &wg) {
-  if (prm.act == 0) return launch_win<BNC, kEpiActNone, kGather>(s, mx, mw, prm, wg);
-  if (prm.act == 1) return launch_win<BNC, kEpiActRelu, kGather>(s, mx, mw, prm, wg);
-  return launch_win<BNC, kEpiActAny, kGather>(s, mx, mw, prm, wg);
+                 const ConvParams &prm, const WinGeom &wg, bool after_prep) {
+  if (prm.act == 0) return launch_win<BNC, kEpiActNone, kGather>(s, mx, mw, prm, wg, after_prep);
+  if (prm.act == 1) return launch_win<BNC, kEpiActRelu, kGather>(s, mx, mw, prm, wg, after_prep);
+  return launch_win<BNC, kEpiActAny, kGather>(s, mx, mw, prm, wg, after_prep);
 }
 
 }  // namespace
@@ -514,7 +534,7 @@ bool conv_window_supported(const ConvParams &p, int n_img) {
 }
 
 int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
-                       const float *x_nhwc, ConvParams prm, int n_img) {
+                       const float *x_nhwc, ConvParams prm, int n_img, bool after_prep) {
   if (!conv_window_supported(prm, n_img)) return kErrUnsupported;
   const bool gather = x_nhwc == nullptr;  // read NCHW prm.x directly
   if (bnc == 64 && n_blocks != 1) return kErrUnsupported;  // pipelines share one slab sequence
@@ -539,11 +559,13 @@ int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp,
   }
   rc = encode_tmap_2d_f32_sw128(&mw, wsplit, kp, n_blocks * 2 * bnc, kp * 4, kConvBK, 2 * bnc);
   if (rc) return rc;
+  // Only the gather form may overlap the preparation: the plane-based form
+  // reads an NHWC plane written by the kernel right before it.
   if (gather)
-    return bnc == 64 ? dispatch_win<64, true>(s, mx, mw, prm, wg)
-                     : dispatch_win<128, true>(s, mx, mw, prm, wg);
-  return bnc == 64 ? dispatch_win<64, false>(s, mx, mw, prm, wg)
-                   : dispatch_win<128, false>(s, mx, mw, prm, wg);
+    return bnc == 64 ? dispatch_win<64, true>(s, mx, mw, prm, wg, after_prep)
+                     : dispatch_win<128, true>(s, mx, mw, prm, wg, after_prep);
+  return bnc == 64 ? dispatch_win<64, false>(s, mx, mw, prm, wg, false)
+                   : dispatch_win<128, false>(s, mx, mw, prm, wg, false);
 }
 
 }  // namespace nplk

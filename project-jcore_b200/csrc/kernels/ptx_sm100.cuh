@@ -107,47 +107,25 @@ __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
-// ---------------------------------------------------------------------------
-// Progress counter in shared memory. An mbarrier wait costs the MMA-issuing
-// thread ~130-200 cycles even when the phase is already complete, which
-// leaves the tensor pipe idle; a helper warp therefore does the mbarrier
-// waits and publishes "items ready" with a release store, and the issuer only
-// polls the counter with acquire loads (~40 cycles when it is ahead).
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void counter_release(uint32_t *ctr, uint32_t v) {
-  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(ctr)), "r"(v)
-               : "memory");
-}
-
-__device__ __forceinline__ uint32_t counter_acquire(const uint32_t *ctr) {
-  uint32_t v;
-  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(ctr))
-               : "memory");
-  return v;
-}
-
-// Waits until *ctr > target. Bounded like mbar_wait.
-__device__ __forceinline__ bool counter_wait(const uint32_t *ctr, uint32_t target,
-                                             volatile int *abort, int *status, int code) {
-  if (counter_acquire(ctr) > target) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (counter_acquire(ctr) > target) return true;
-    if ((it & 255u) == 0u) {
-      if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        *abort = 1;
-        atomicCAS(status, 0, code);
-        return false;
-      }
-    }
-  }
-}
-
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor-core operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while the previous kernel in the stream still
+// runs; griddep_wait() blocks until that kernel has completed and its
+// writes are visible (a no-op for a normally launched kernel), and
+// griddep_launch_dependents() lets the next kernel start early.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
