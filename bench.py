@@ -381,6 +381,70 @@ def run_b200(args, rank, world, local_rank):
     return lib, result
 
 
+def bandwidth_also(lib, local_rank, reps=10):
+    """The bandwidth-bound primitives on one GPU, each on tensors larger than
+    L2 (N=256, C=512, 14x14 NCHW = 103 MB; LN on 8192 x 4096; softmax over
+    102400 rows of 1000):
+    median CUDA-event time of `reps` launches with L2 flushed before each,
+    algorithmic bytes (each input read once, each output written once) per
+    second and the fraction of the measured HBM copy bandwidth."""
+    import torch
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    n, c, hw = 256, 512, 14
+    x = torch.randn(n, c, hw, hw, device=dev, generator=gen)
+    y = torch.empty_like(x)
+    w = torch.randn(c, 1, 3, 3, device=dev, generator=gen) * 0.3
+    bn = [torch.rand(c, device=dev, generator=gen) + 0.5 for _ in range(4)]
+    gap = torch.empty(n * c, device=dev)
+    pooled = torch.empty(n, c, 7, 7, device=dev)
+    rows = torch.randn(8192, 4096, device=dev, generator=gen)
+    rows_y = torch.empty_like(rows)
+    logits = torch.randn(102400, 1000, device=dev, generator=gen)
+    probs = torch.empty_like(logits)
+    g = nb.conv_geom(n, c, hw, hw, c, 3, 3, 1, 1)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+    nx = x.numel()
+    cases = [
+        ("depthwise 3x3", nx * 8 + w.numel() * 4,
+         lambda: lib.nplk_depthwise_conv2d(s, C.byref(g), p(x), p(w), None, p(y))),
+        ("batch_norm inference", nx * 8,
+         lambda: lib.nplk_batch_norm_infer(s, n, c, hw * hw, p(x), p(y), p(bn[0]), p(bn[1]),
+                                           p(bn[2]), p(bn[3]), 1e-5)),
+        ("relu", nx * 8, lambda: lib.nplk_activation(s, nx, p(x), p(y), 1, 0.0, 0)),
+        ("max pool 3x3/s2", nx * 4 + pooled.numel() * 4,
+         lambda: lib.nplk_pool2d(s, n, c, hw, hw, 3, 3, 2, 2, 1, 1, 7, 7, 0, 0, p(x),
+                                 p(pooled))),
+        ("global avg pool", nx * 4 + gap.numel() * 4,
+         lambda: lib.nplk_global_avg_pool(s, n * c, hw * hw, p(x), p(gap))),
+        ("softmax rows of 1000", logits.numel() * 8,
+         lambda: lib.nplk_softmax(s, 102400, 1000, 1, p(logits), p(probs))),
+        ("layer_norm 8192x4096", rows.numel() * 8,
+         lambda: lib.nplk_layer_norm(s, 8192, 4096, p(rows), p(rows_y), None, None, 1e-5)),
+    ]
+    hbm, _, src = measured_peaks()
+    out = {}
+    for name, nbytes, fn in cases:
+        assert fn() == 0
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            assert fn() == 0
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ms = statistics.median(ts)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 1), "bytes": int(nbytes), "GB/s": round(gbs, 1),
+                     "frac_of_hbm": round(gbs / hbm, 3)}
+    out["peak"] = f"{src} HBM copy {hbm} GB/s"
+    return out
+
+
 def gemm_also(lib, args, local_rank):
     """Large-GEMM figure on one GPU: C = A@B + C (C pre-filled with the bias row)."""
     import torch
@@ -544,7 +608,8 @@ def main():
                 result["also"] = {"gemm_column_sharded": gd}
         if rank == 0:
             if world == 1 and not args.no_gemm:
-                result["also"] = {"gemm": gemm_also(lib, args, local_rank)}
+                result["also"] = {"gemm": gemm_also(lib, args, local_rank),
+                                  "bandwidth": bandwidth_also(lib, local_rank)}
             if world == 1:
                 r = reference_cpu(3, 1)
                 if r is not None:

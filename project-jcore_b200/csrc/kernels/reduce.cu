@@ -192,11 +192,43 @@ __global__ void layernorm_generic_kernel(const float *__restrict__ x, float *__r
 // ---------------------------------------------------------------------------
 // Global average pool: one warp per contiguous plane of hw elements.
 // ---------------------------------------------------------------------------
+// A warp reduces kGapPlanes planes per iteration, issuing all their loads
+// before the reductions, so several 16-byte loads per lane are in flight.
+constexpr int kGapPlanes = 4;
+
 __global__ void gap_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t planes,
                            int64_t hw, bool vec) {
   const int lane = threadIdx.x & 31;
   const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  if (vec && hw <= 4 * 32 * 4) {
+    // Planes of at most 512 elements: up to 4 float4 per lane per plane.
+    const int64_t hw4 = hw / 4;
+    for (int64_t p0 = warp_id * kGapPlanes; p0 < planes; p0 += nwarps * kGapPlanes) {
+      float s[kGapPlanes];
+#pragma unroll
+      for (int k = 0; k < kGapPlanes; ++k) {
+        s[k] = 0.0f;
+        if (p0 + k < planes) {
+          const float4 *x4 = reinterpret_cast<const float4 *>(x + (p0 + k) * hw);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int64_t idx = lane + 32 * j;
+            if (idx < hw4) {
+              const float4 v = __ldg(x4 + idx);
+              s[k] += (v.x + v.y) + (v.z + v.w);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kGapPlanes; ++k) {
+        const float t = warp_sum(s[k]);
+        if (lane == 0 && p0 + k < planes) y[p0 + k] = t / static_cast<float>(hw);
+      }
+    }
+    return;
+  }
   for (int64_t p = warp_id; p < planes; p += nwarps) {
     const float *xp = x + p * hw;
     float s = 0.0f;
