@@ -487,12 +487,121 @@ def gemm_also(lib, args, local_rank):
     rows = torch.arange(0, GEMM_M, GEMM_M // 8, device=dev)
     ref = A[rows].double() @ B.double() + bias.double()
     err = ((Cm[rows].double() - ref).abs().max() / ref.abs().max()).item()
-    del A, B, Cm, work
+    # The whole large-GEMM workload: bias (beta = 1) and ReLU in the GEMM
+    # epilogue, then layer norm over rows of 16384.
+    Y = torch.empty_like(Cm)
+    pipe_ms, ln_ms = [], []
+    for _ in range(n):
+        Cm.copy_(bias.expand(GEMM_M, GEMM_N))
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        r = lib.nplk_gemm(sptr, GEMM_M, GEMM_N, GEMM_K, 1.0, p(A), GEMM_K, p(B), GEMM_N, 1.0,
+                          p(Cm), GEMM_N, None, nb.NPL_ACT_RELU, 0.0, 0, p(work), ws, None)
+        assert r == 0, r
+        e1.record(stream)
+        r = lib.nplk_layer_norm(sptr, GEMM_M, GEMM_N, p(Cm), p(Y), None, None, 1e-5)
+        assert r == 0, r
+        e2.record(stream)
+        torch.cuda.synchronize()
+        pipe_ms.append(e0.elapsed_time(e2))
+        ln_ms.append(e1.elapsed_time(e2))
+    pm, lm = statistics.mean(pipe_ms), statistics.mean(ln_ms)
+    del A, B, Cm, Y, work
     torch.cuda.empty_cache()
     return {"workload": "npl_matmul fp32 [8192x4096]@[4096x16384] + bias (beta=1), 1 GPU",
             "value": round(GEMM_FLOPS / (ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
             "ms_per_step": round(ms, 4), "normwise_err_sampled_rows": err,
-            "step": "split A and B^T into tf32 hi/lo + tcgen05 GEMM"}
+            "step": "split A and B^T into tf32 hi/lo + tcgen05 GEMM",
+            "with_relu_and_layer_norm": {
+                "ms": round(pm, 4), "TFLOP/s (GEMM flops)": round(GEMM_FLOPS / (pm / 1e3) / 1e12, 2),
+                "layer_norm_ms": round(lm, 4),
+                "layer_norm_GB/s": round(2 * GEMM_M * GEMM_N * 4 / (lm / 1e3) / 1e9, 1),
+                "step": "GEMM with bias (beta=1) and ReLU in the epilogue, then layer norm "
+                        "over rows of 16384 (gamma 1, beta 0, eps 1e-5)"}}
+
+
+def stem_also(lib, local_rank, reps=5):
+    """The stem layer on one GPU: conv 7x7/s2/p3 3->64 on [128,3,224,224]
+    (C_in = 3: the direct-gather kernel) with BN + ReLU, then max pool
+    3x3/s2/p1 -> [128,64,56,56]; inputs U[-1,1], w N(0, sqrt(2/147))."""
+    import torch
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    n = 128
+    x = torch.rand(n, 3, 224, 224, device=dev, generator=gen) * 2 - 1
+    w = torch.randn(64, 3, 7, 7, device=dev, generator=gen) * (2.0 / 147) ** 0.5
+    bn = [torch.rand(64, device=dev, generator=gen) + 0.5 for _ in range(4)]
+    y = torch.empty(n, 64, 112, 112, device=dev)
+    pooled = torch.empty(n, 64, 56, 56, device=dev)
+    g = nb.conv_geom(n, 3, 224, 224, 64, 7, 7, 2, 3)
+    ws = lib.nplk_conv_workspace_size(C.byref(g))
+    work = torch.empty(ws // 4 + 64, device=dev)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+
+    def conv():
+        r = lib.nplk_conv2d_fused(s, C.byref(g), p(x), p(w), None, p(bn[0]), p(bn[1]), p(bn[2]),
+                                  p(bn[3]), 1e-5, nb.NPL_ACT_RELU, 0.0, p(y), p(work), ws, None)
+        assert r == 0, r
+
+    def pool():
+        r = lib.nplk_pool2d(s, n, 64, 112, 112, 3, 3, 2, 2, 1, 1, 56, 56, 0, 0, p(y), p(pooled))
+        assert r == 0, r
+
+    conv(), pool()
+    cms, pms = [], []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        conv()
+        e1.record()
+        pool()
+        e2.record()
+        torch.cuda.synchronize()
+        cms.append(e0.elapsed_time(e1))
+        pms.append(e1.elapsed_time(e2))
+    if lib.nplk_read_status(s) != 0:
+        raise RuntimeError("conv kernel reported a pipeline timeout")
+    flops = 2.0 * n * 64 * 3 * 112 * 112 * 49
+    cm, pm = statistics.median(cms), statistics.median(pms)
+    return {"workload": "conv 7x7/s2/p3 3->64 [128,3,224,224] + BN + ReLU, then max pool "
+                        "3x3/s2/p1", "conv_ms": round(cm, 4),
+            "conv_TFLOP/s": round(flops / (cm / 1e3) / 1e12, 2), "pool_ms": round(pm, 4),
+            "pool_GB/s": round((y.numel() + pooled.numel()) * 4 / (pm / 1e3) / 1e9, 1)}
+
+
+def gemm1024_also(lib, local_rank, reps=20):
+    """npl_matmul 1024 x 1024 x 1024 (A, B ~ U[-1,1], beta 0) on device
+    pointers: median CUDA-event time of nplk_gemm (split + GEMM)."""
+    import torch
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    m = 1024
+    a = torch.rand(m, m, device=dev, generator=gen) * 2 - 1
+    b = torch.rand(m, m, device=dev, generator=gen) * 2 - 1
+    c = torch.empty(m, m, device=dev)
+    ws = lib.nplk_gemm_workspace_size(m, m, m)
+    work = torch.empty(ws // 4 + 64, device=dev)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    ts = []
+    for i in range(reps + 3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = lib.nplk_gemm(s, m, m, m, 1.0, p(a), m, p(b), m, 0.0, p(c), m, None, 0, 0.0, 0,
+                          p(work), ws, None)
+        assert r == 0, r
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            ts.append(e0.elapsed_time(e1))
+    ms = statistics.median(ts)
+    err = ((c.double() - a.double() @ b.double()).abs().max() /
+           (a.double() @ b.double()).abs().max()).item()
+    return {"workload": "npl_matmul 1024^3", "us": round(ms * 1e3, 2),
+            "TFLOP/s": round(2 * m ** 3 / (ms / 1e3) / 1e12, 2), "normwise_err": err}
 
 
 def gemm_dist(args, rank, world, local_rank):
@@ -609,6 +718,8 @@ def main():
         if rank == 0:
             if world == 1 and not args.no_gemm:
                 result["also"] = {"gemm": gemm_also(lib, args, local_rank),
+                                  "gemm_1024": gemm1024_also(lib, local_rank),
+                                  "stem": stem_also(lib, local_rank),
                                   "bandwidth": bandwidth_also(lib, local_rank)}
             if world == 1:
                 r = reference_cpu(3, 1)

@@ -471,24 +471,12 @@ int launch_win(cudaStream_t s, const CUtensorMap &mx, const CUtensorMap &mw,
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  if (after_prep) {
+  if (after_prep)
     // Overlap with the weight preparation launched just before: the gather
     // warps only read x (complete before the preparation started); the slab
     // producer and the epilogue wait for the preparation's writes.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(T::kThreads);
-    cfg.dynamicSmemBytes = T::kSmemBytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, mx, mw, prm, wg);
-    count_launch();
-    return map_cuda_error(e);
-  }
+    return launch_programmatic(kernel, dim3(grid), dim3(T::kThreads), T::kSmemBytes, s, mx, mw,
+                               prm, wg);
   kernel<<<grid, T::kThreads, T::kSmemBytes, s>>>(mx, mw, prm, wg);
   count_launch();
   return launch_result();

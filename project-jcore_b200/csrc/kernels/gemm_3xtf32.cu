@@ -117,6 +117,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      griddep_wait();  // the split operands come from the kernels just before
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -316,9 +317,8 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
   if (rc) return rc;
   const int64_t tiles = g.m_blocks * g.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  gemm_3xtf32_kernel<BN><<<grid, kGemmThreads, T::kSmemBytes, stream>>>(map_a, map_b, prm);
-  count_launch();
-  return launch_result();
+  return launch_programmatic(gemm_3xtf32_kernel<BN>, dim3(grid), dim3(kGemmThreads),
+                             T::kSmemBytes, stream, map_a, map_b, prm);
 }
 
 }  // namespace
@@ -328,7 +328,8 @@ int launch_split_rows(cudaStream_t s, const float *src, int64_t rows, int64_t co
                       int64_t col_offset, float *dst, int row_block, int64_t kp,
                       int64_t rows_pad);
 int launch_split_transpose(cudaStream_t s, const float *src, int64_t krows, int64_t ncols,
-                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad);
+                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad,
+                           bool overlap_previous = false);
 
 }  // namespace nplk
 
@@ -360,7 +361,10 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
 
   int rc = launch_split_rows(s, A, M, K, lda, 0, a_split, kGemmBM, g.kp, g.m_blocks * kGemmBM);
   if (rc) return rc;
-  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn);
+  // The B split overlaps the A split and the GEMM kernel's set-up overlaps
+  // both (programmatic dependent launch); the GEMM's TMA producer waits for
+  // the splits before its first load.
+  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn, true);
   if (rc) return rc;
 
   GemmParams prm{};

@@ -4,8 +4,8 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <map>
 #include <mutex>
-#include <set>
 #include <utility>
 
 namespace nplk {
@@ -93,16 +93,19 @@ void count_launch(uint64_t n) { t_launches += n; }
 int launch_result() { return map_cuda_error(cudaGetLastError()); }
 
 int ensure_dynamic_smem(const void *func, int bytes) {
+  // The attribute is raised, never lowered: a kernel launched with several
+  // shared-memory sizes keeps the largest one set so far.
   static std::mutex mu;
-  static std::set<std::pair<int, const void *>> done;
+  static std::map<std::pair<int, const void *>, int> set_bytes;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kErrInternal;
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count({dev, func})) return kOk;
+  auto it = set_bytes.find({dev, func});
+  if (it != set_bytes.end() && it->second >= bytes) return kOk;
   cudaError_t e =
       cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return map_cuda_error(e);
-  done.insert({dev, func});
+  set_bytes[{dev, func}] = bytes;
   return kOk;
 }
 

@@ -55,6 +55,26 @@ int encode_tmap_im2col_nhwc_f32_sw128(CUtensorMap *map, const void *base, uint64
                                      int lower_h, int upper_w, int upper_h, uint32_t stride_w,
                                      uint32_t stride_h, uint32_t channels, uint32_t pixels);
 
+// Launches `kernel` with programmatic stream serialization: it may start
+// while the previous kernel in the stream is still running and must call
+// griddep_wait() before reading what that kernel writes. Counts the launch.
+template <typename... KArgs, typename... Args>
+int launch_programmatic(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                        cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  count_launch();
+  return map_cuda_error(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 

@@ -19,6 +19,7 @@ namespace nplk {
 __global__ void split_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                   int64_t ld, int64_t col_offset, float *__restrict__ dst,
                                   int row_block_shift, int64_t kp, int64_t rows_pad) {
+  griddep_launch_dependents();  // the B split and the GEMM may start meanwhile
   const int64_t k = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (k >= kp) return;
   const int64_t row_block = int64_t(1) << row_block_shift;
@@ -47,6 +48,7 @@ __global__ void split_transpose_kernel(const float *__restrict__ src, int64_t kr
                                        int64_t ncols, int64_t ld, float *__restrict__ dst,
                                        int row_block_shift, int64_t kp, int64_t npad) {
   __shared__ float tile[32][33];
+  griddep_launch_dependents();
   const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
   const int64_t row_block = int64_t(1) << row_block_shift;
   for (int64_t n0 = static_cast<int64_t>(blockIdx.y) * 32; n0 < npad;
@@ -73,6 +75,9 @@ __global__ void split_transpose_kernel(const float *__restrict__ src, int64_t kr
     }
     __syncthreads();
   }
+  // When launched to overlap the A split before it, finish only after it:
+  // the GEMM behind waits for this grid, and so for both splits.
+  griddep_wait();
 }
 
 static int log2_exact(int v) {
@@ -96,7 +101,8 @@ int launch_split_rows(cudaStream_t s, const float *src, int64_t rows, int64_t co
 }
 
 int launch_split_transpose(cudaStream_t s, const float *src, int64_t krows, int64_t ncols,
-                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad) {
+                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad,
+                           bool overlap_previous) {
   const int shift = log2_exact(row_block);
   if (shift < 0 || kp % 32 != 0 || npad % 32 != 0 || npad % row_block != 0)
     return kErrInvalidArg;
@@ -104,8 +110,11 @@ int launch_split_transpose(cudaStream_t s, const float *src, int64_t krows, int6
   int64_t gy = npad / 32;
   if (gy > 65535) gy = 65535;
   if (gx > 2147483647) return kErrUnsupported;
-  split_transpose_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
-                           dim3(32, 8), 0, s>>>(src, krows, ncols, ld, dst, shift, kp, npad);
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  if (overlap_previous)
+    return launch_programmatic(split_transpose_kernel, grid, dim3(32, 8), 0, s, src, krows, ncols,
+                               ld, dst, shift, kp, npad);
+  split_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(src, krows, ncols, ld, dst, shift, kp, npad);
   count_launch();
   return launch_result();
 }

@@ -1,7 +1,7 @@
 // Sliding-window kernels over NCHW planes: depthwise convolution and max /
 // average pooling.
 //
-// plane_window_kernel (planes of at most 12 K elements): a CTA stages a batch
+// plane_window_kernel (planes of at most 24 K elements): a CTA stages a batch
 // of whole input planes in shared memory with 16-byte loads (consecutive
 // planes are contiguous in NCHW, so the batch is one contiguous range and
 // many bytes are in flight per SM), then each thread computes 4 adjacent
@@ -173,7 +173,7 @@ __device__ __forceinline__ float window_out(const float *xp, const float *wp, in
 }
 
 constexpr int kPlaneBatchBytes = 20480;   // staged input per CTA batch (target)
-constexpr int kPlaneMaxBytes = 49152;     // largest plane staged whole
+constexpr int kPlaneMaxBytes = 98304;     // largest plane staged whole (2 buffers)
 
 // Asynchronous global -> shared copies (cp.async), so that the next batch of
 // planes loads while the current one is computed.
