@@ -20,6 +20,7 @@ enum : int {
   kStatusTimeoutMma = 102,       // MMA warp waited too long for a filled stage
   kStatusTimeoutEpilogue = 103,  // epilogue waited too long for an accumulator
   kStatusTimeoutAccFree = 104,   // MMA warp waited too long for a drained accumulator
+  kStatusTimeoutStage = 105,     // window kernel warp waited too long for a staged batch
 };
 
 // 4 s of device time: orders of magnitude above any legitimate stage wait.

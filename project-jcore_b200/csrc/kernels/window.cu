@@ -1,22 +1,25 @@
 // Sliding-window kernels over NCHW planes: depthwise convolution and max /
 // average pooling.
 //
-// plane_window_kernel (planes of at most 24 K elements): a CTA stages a batch
-// of whole input planes in shared memory with 16-byte loads (consecutive
-// planes are contiguous in NCHW, so the batch is one contiguous range and
-// many bytes are in flight per SM), then each thread computes 4 adjacent
-// outputs of one row from shared memory. window_kernel (larger planes): one
-// thread per output, consecutive threads on consecutive output columns, so
-// the window reads of a warp hit a few cache lines and are served from L1
-// after the first touch. Both compute every output with the same expression
-// in the same order (the reference's: kh outer, kw inner, padded cells
-// skipped), so they agree bit for bit; each input element crosses HBM about
-// once.
+// band_window_kernel (rows of up to 2 K elements): a CTA stages a batch of
+// input in shared memory with 16-byte cp.async copies -- several whole planes
+// when a plane is small (consecutive planes are contiguous in NCHW), else a
+// band of rows of one plane -- while it computes the previous batch; each
+// thread computes a column of outputs and consecutive lanes store consecutive
+// columns. window_kernel
+// (wider rows): one thread per output, consecutive threads on consecutive
+// output columns, so the window reads of a warp hit a few cache lines and are
+// served from L1 after the first touch. Every output takes the reference's
+// order (kh outer, kw inner, padded cells skipped -- the 3x3 path combines
+// the operation's identity there instead, which leaves each result bit for
+// bit the same), so all paths agree exactly; each input element crosses HBM
+// about once.
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
 #include "nplk_device.cuh"
 #include "nplk_host.h"
+#include "ptx_sm100.cuh"
 
 namespace nplk {
 
@@ -113,38 +116,34 @@ __global__ void pool_kernel(const float *__restrict__ x, float *__restrict__ y, 
 }
 
 // One output of window operation kOp (0 depthwise, 1 max pool, 2 average
-// pool) at (oh, ow) of a plane read from xp (row pitch g.W); wp: the plane's
-// filter (depthwise). Same expression and order as dwconv_kernel /
-// pool_kernel.
-template <int kOp, int KH_, int KW_>
+// pool) at (oh, ow) of a plane staged in shared memory from input row ih_lo
+// on (row pitch g.W); wp: the plane's filter (depthwise). Same expression and
+// order as dwconv_kernel / pool_kernel.
+template <int kOp>
 __device__ __forceinline__ float window_out(const float *xp, const float *wp, int oh, int ow,
-                                            const WindowGeom &g, int count_include_pad) {
-  const int KH = KH_ ? KH_ : g.KH, KW = KW_ ? KW_ : g.KW;
+                                            const WindowGeom &g, int count_include_pad,
+                                            int ih_lo) {
   if (kOp == 0) {
     float sum = 0.0f;
-#pragma unroll
-    for (int kh = 0; kh < KH; ++kh) {
+    for (int kh = 0; kh < g.KH; ++kh) {
       const int ih = oh * g.sh + kh - g.ph;
       if (static_cast<unsigned>(ih) >= static_cast<unsigned>(g.H)) continue;
-#pragma unroll
-      for (int kw = 0; kw < KW; ++kw) {
+      for (int kw = 0; kw < g.KW; ++kw) {
         const int iw = ow * g.sw + kw - g.pw;
         if (static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
-          sum += xp[ih * g.W + iw] * wp[kh * KW + kw];
+          sum += xp[(ih - ih_lo) * g.W + iw] * wp[kh * g.KW + kw];
       }
     }
     return sum;
   } else if (kOp == 1) {
     float m = -CUDART_INF_F;
-#pragma unroll
-    for (int kh = 0; kh < KH; ++kh) {
+    for (int kh = 0; kh < g.KH; ++kh) {
       const int ih = oh * g.sh + kh - g.ph;
       if (static_cast<unsigned>(ih) >= static_cast<unsigned>(g.H)) continue;
-#pragma unroll
-      for (int kw = 0; kw < KW; ++kw) {
+      for (int kw = 0; kw < g.KW; ++kw) {
         const int iw = ow * g.sw + kw - g.pw;
         if (static_cast<unsigned>(iw) < static_cast<unsigned>(g.W)) {
-          const float v = xp[ih * g.W + iw];
+          const float v = xp[(ih - ih_lo) * g.W + iw];
           m = (m < v) ? v : m;  // std::max(m, v)
         }
       }
@@ -153,15 +152,13 @@ __device__ __forceinline__ float window_out(const float *xp, const float *wp, in
   } else {
     float s = 0.0f;
     int cnt = 0;
-#pragma unroll
-    for (int kh = 0; kh < KH; ++kh) {
+    for (int kh = 0; kh < g.KH; ++kh) {
       const int ih = oh * g.sh + kh - g.ph;
       const bool row_in = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
-#pragma unroll
-      for (int kw = 0; kw < KW; ++kw) {
+      for (int kw = 0; kw < g.KW; ++kw) {
         const int iw = ow * g.sw + kw - g.pw;
         if (row_in && static_cast<unsigned>(iw) < static_cast<unsigned>(g.W)) {
-          s += xp[ih * g.W + iw];
+          s += xp[(ih - ih_lo) * g.W + iw];
           ++cnt;
         } else if (count_include_pad) {
           ++cnt;
@@ -172,227 +169,414 @@ __device__ __forceinline__ float window_out(const float *xp, const float *wp, in
   }
 }
 
-constexpr int kPlaneBatchBytes = 20480;   // staged input per CTA batch (target)
-constexpr int kPlaneMaxBytes = 98304;     // largest plane staged whole (2 buffers)
-
-// Asynchronous global -> shared copies (cp.async), so that the next batch of
-// planes loads while the current one is computed.
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
+// Bulk copy of `bytes` (a multiple of 16) from global to shared memory on the
+// async proxy; completion is counted on `bar` (transaction bytes).
+__device__ __forceinline__ void bulk_load_g2s(void *dst, const void *src, uint32_t bytes,
+                                              uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-               "l"(src)
-               : "memory");
+constexpr int kBandWarps = 4;                      // consumer warps per CTA
+constexpr int kBandThreads = (kBandWarps + 1) * 32;  // + one producer warp
+constexpr int kBandStages = 8;                     // staged batches per CTA
+constexpr int kBandStageBytes = 7136;              // per stage: 4 CTAs (57 KB) per SM
+constexpr int kBandItemsMax = 64;                  // items per batch: two per lane
+
+// Output rows per item of the 3x3 path: 14 at vertical stride 1, 7 at 2 (they
+// divide the usual plane heights 7, 14, 28, 56, 112); an item covers two
+// adjacent output columns.
+template <int SH_>
+struct StripRows {
+  static constexpr int value = SH_ == 1 ? 14 : 7;
+};
+
+// Work plan of band_window_kernel. A batch is either np whole planes (whole:
+// consecutive NCHW planes are one contiguous range) or one band of R output
+// rows of one plane (its input rows are one contiguous range too).
+struct BandPlan {
+  int whole, np, R, bands;
+  int strips;          // strips per plane (whole planes)
+  int stage_floats;    // one stage (multiple of 4 floats)
+  FastDiv div_pairs;   // by the output column pairs of a row
+  FastDiv div_strips;  // by strips
+  int64_t batches;
+};
+
+struct BandBatch {
+  int64_t q0;  // first plane
+  int cnt;     // planes
+  int oh0, oh1, ih_lo, ih_hi;
+};
+
+__device__ __forceinline__ BandBatch band_batch(int64_t b, int64_t planes, const BandPlan &bp,
+                                                const WindowGeom &g, int KH) {
+  BandBatch r;
+  if (bp.whole) {
+    r.q0 = b * bp.np;
+    r.cnt = static_cast<int>(planes - r.q0 < bp.np ? planes - r.q0 : bp.np);
+    r.oh0 = 0;
+    r.oh1 = g.Ho;
+    r.ih_lo = 0;
+    r.ih_hi = g.H;
+  } else {
+    r.q0 = b / bp.bands;
+    const int band = static_cast<int>(b - r.q0 * bp.bands);
+    r.cnt = 1;
+    r.oh0 = band * bp.R;
+    r.oh1 = min(g.Ho, r.oh0 + bp.R);
+    r.ih_lo = max(0, r.oh0 * g.sh - g.ph);
+    r.ih_hi = min(g.H, (r.oh1 - 1) * g.sh - g.ph + KH);
+    if (r.ih_hi < r.ih_lo) r.ih_hi = r.ih_lo;
+  }
+  return r;
 }
 
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
+// First input element of a batch and how many follow it contiguously.
+__device__ __forceinline__ const float *band_src(const float *x, const BandBatch &bb, int HW,
+                                                 int W, int &n_in) {
+  n_in = (bb.cnt - 1) * HW + (bb.ih_hi - bb.ih_lo) * W;
+  return x + bb.q0 * HW + static_cast<int64_t>(bb.ih_lo) * W;
 }
 
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// SW_ (1 or 2): horizontal stride of the 3x3 depthwise fast path, fixed at
-// compile time so that its input patch stays in registers; 0 otherwise.
-template <int kOp, int KH_, int KW_, int SW_>
-__global__ void __launch_bounds__(256) plane_window_kernel(const float *__restrict__ x,
-                                                           const float *__restrict__ w,
-                                                           const float *__restrict__ bias,
-                                                           float *__restrict__ y, int64_t planes,
-                                                           int np, WindowGeom g,
-                                                           int count_include_pad, int vec) {
-  // Two buffers, each: np input planes, then np filters (depthwise).
-  extern __shared__ float smem_planes[];
-  const int KH = KH_ ? KH_ : g.KH, KW = KW_ ? KW_ : g.KW;
-  const int taps = KH * KW;
-  const int HW = g.H * g.W, HoWo = g.Ho * g.Wo;
-  const int groups = (g.Wo + 3) >> 2;  // items of 4 outputs per output row
-  const int items_pp = g.Ho * groups;
-  const int buf_floats = (np * (HW + (kOp == 0 ? taps : 0)) + 3) & ~3;
-  const int t = threadIdx.x;
-  // Issues the asynchronous copies of the batch starting at plane q0.
-  auto stage = [&](int64_t q0, float *buf) {
-    const int cnt = static_cast<int>(planes - q0 < np ? planes - q0 : np);
-    const float *src = x + q0 * HW;
-    const int n_in = cnt * HW;
-    if (vec) {
-      const float4 *s4 = reinterpret_cast<const float4 *>(src);
-      float4 *d4 = reinterpret_cast<float4 *>(buf);
-      for (int i = t; i < (n_in >> 2); i += 256) cp_async16(d4 + i, s4 + i);
-    } else {
-      for (int i = t; i < n_in; i += 256) cp_async4(buf + i, src + i);
+// Sliding-window operation kOp over NCHW planes. Warp-specialised: one lane of
+// the last warp stages batches (whole planes or row bands, each one
+// contiguous range of x) into a ring of kBandStages shared-memory stages with
+// one bulk copy each -- the 16-byte-aligned superset of the range, which lies
+// on the same mapped pages -- completing on the stage's mbarrier; each of the
+// kBandWarps consumer warps computes whole batches (every kBandWarps-th of
+// the CTA's) and releases the stage. No CTA-wide barrier: a warp waits only
+// for its own batch, and up to kBandStages batches are in flight per CTA.
+// SH_, SW_ > 0: 3x3 window with those strides; an item is two adjacent output
+// columns over a strip of StripRows<SH_> output rows, so every input row
+// under the strip is read from shared memory once, consecutive lanes read
+// consecutive columns and each tap is one unconditional combine. SH_ = SW_ =
+// 0: any window, one output per item. Outputs are stored straight from
+// registers (consecutive lanes on consecutive columns). Bounded waits record
+// kStatusTimeoutProducer / kStatusTimeoutStage in *status.
+template <int kOp, int SH_, int SW_>
+__global__ void __launch_bounds__(kBandThreads, 4) band_window_kernel(
+    const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ bias,
+    float *__restrict__ y, int64_t planes, BandPlan bp, WindowGeom g, int count_include_pad,
+    int *status) {
+  extern __shared__ __align__(128) uint8_t smem_band[];
+  float *stages = reinterpret_cast<float *>(smem_band);
+  uint64_t *full = reinterpret_cast<uint64_t *>(stages + kBandStages * bp.stage_floats);
+  uint64_t *empty = full + kBandStages;
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kBandStages);
+  constexpr bool kFast = SH_ > 0;
+  const int KH = kFast ? 3 : g.KH;
+  const int taps = kFast ? 9 : g.KH * g.KW;
+  const int HW = g.H * g.W;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBandStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-    if (kOp == 0) {
-      float *wb = buf + np * HW;
-      for (int i = t; i < cnt * taps; i += 256) {
-        const int pl = i / taps;
-        const int c = static_cast<int>((q0 + pl) % g.C);
-        cp_async4(wb + i, w + static_cast<int64_t>(c) * taps + (i - pl * taps));
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // This CTA's batches: blockIdx.x + k * gridDim.x, k < nk.
+  const int64_t nk = bp.batches > blockIdx.x
+                         ? (bp.batches - 1 - blockIdx.x) / gridDim.x + 1
+                         : 0;
+
+  if (warp == kBandWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int64_t k = 0;
+      for (; k < nk; ++k) {
+        const int s = static_cast<int>(k % kBandStages);
+        const uint32_t ph = static_cast<uint32_t>(k / kBandStages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) break;
+        const BandBatch bb = band_batch(blockIdx.x + k * gridDim.x, planes, bp, g, KH);
+        int n_in;
+        const float *src = band_src(x, bb, HW, g.W, n_in);
+        const uintptr_t lo = reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15);
+        const uintptr_t hi = (reinterpret_cast<uintptr_t>(src + n_in) + 15) & ~uintptr_t(15);
+        // A batch with no input rows (a band inside the padding) copies
+        // nothing: its src may lie past the end of x.
+        const uint32_t bytes = n_in > 0 ? static_cast<uint32_t>(hi - lo) : 0u;
+        if (bytes > 0) {
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_load_g2s(stages + s * bp.stage_floats, reinterpret_cast<const void *>(lo), bytes,
+                        &full[s]);
+        } else {
+          mbar_arrive(&full[s]);
+        }
+      }
+      // Let the last copies land before the CTA can exit (they already have
+      // unless the CTA aborted).
+      for (int64_t j = k > kBandStages ? k - kBandStages : 0; j < k; ++j)
+        mbar_drain(&full[j % kBandStages], static_cast<uint32_t>(j / kBandStages) & 1u);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  for (int64_t k = warp; k < nk; k += kBandWarps) {
+    const int s = static_cast<int>(k % kBandStages);
+    const uint32_t ph = static_cast<uint32_t>(k / kBandStages) & 1u;
+    const BandBatch bb = band_batch(blockIdx.x + k * gridDim.x, planes, bp, g, KH);
+    const int rows = bb.oh1 - bb.oh0;
+    const int c0 = kOp == 0 ? static_cast<int>(bb.q0 % g.C) : 0;  // channel of the first plane
+    // The 3x3 path: this lane's first item and its filter, loaded from global
+    // memory before the wait for the staged input so that the two overlap.
+    constexpr int Vf = kFast ? StripRows<SH_ ? SH_ : 1>::value : 1;
+    const int strips = bp.whole ? bp.strips : (rows + Vf - 1) / Vf;
+    const int pairs = (g.Wo + 1) >> 1;
+    int rest0 = 0, pl0 = 0;
+    float wnext[9];
+    if (kFast) {
+      rest0 = static_cast<int>(fdiv(static_cast<uint32_t>(lane), bp.div_pairs));
+      pl0 = bp.whole ? static_cast<int>(fdiv(static_cast<uint32_t>(rest0), bp.div_strips)) : 0;
+      if (kOp == 0 && pl0 < bb.cnt) {
+        const float *wp = w + ((c0 + pl0) % g.C) * 9;
+#pragma unroll
+        for (int k9 = 0; k9 < 9; ++k9) wnext[k9] = __ldg(wp + k9);
       }
     }
-    cp_async_commit();
-  };
-  const int64_t step = static_cast<int64_t>(gridDim.x) * np;
-  int64_t p0 = static_cast<int64_t>(blockIdx.x) * np;
-  if (p0 < planes) stage(p0, smem_planes);
-  int cur = 0;
-  for (; p0 < planes; p0 += step, cur ^= 1) {
-    float *sp = smem_planes + cur * buf_floats;
-    float *sw = sp + np * HW;
-    const int cnt = static_cast<int>(planes - p0 < np ? planes - p0 : np);
-    if (p0 + step < planes) {
-      stage(p0 + step, smem_planes + (cur ^ 1) * buf_floats);
-      cp_async_wait<1>();  // this batch landed; the next one may still be in flight
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (kOp == 0 && KH_ == 3 && KW_ == 3 && SW_ > 0) {
-      // 3x3 depthwise: threads are split evenly over the batch's planes, so a
-      // thread keeps its plane's 9 weights in registers; an item of 4
-      // adjacent outputs reads its 3 x (3*sw + 3) input patch once.
-      const int tpp = 256 / np;
-      const int pl = t / tpp;
-      if (pl < cnt) {
-        const float *xp = sp + pl * HW;
-        const float *wp = sw + pl * 9;
+    if (!mbar_wait(&full[s], ph, abort_flag, status, kStatusTimeoutStage)) break;
+    int n_in;
+    const float *src = band_src(x, bb, HW, g.W, n_in);
+    const float *data = stages + s * bp.stage_floats +
+                        static_cast<int>((reinterpret_cast<uintptr_t>(src) >> 2) & 3);
+    float *out = y + bb.q0 * (static_cast<int64_t>(g.Ho) * g.Wo) +
+                 static_cast<int64_t>(bb.oh0) * g.Wo;
+    if constexpr (kFast) {
+      constexpr int V = StripRows<SH_>::value;
+      constexpr int kCols = SW_ + 3;            // input columns under two outputs
+      constexpr int kRows = (V - 1) * SH_ + 3;  // input rows under a strip
+      const int items = bb.cnt * strips * pairs;
+      for (int it = lane; it < items; it += 32) {
+        const bool first = it == lane;
+        const int rest =
+            first ? rest0 : static_cast<int>(fdiv(static_cast<uint32_t>(it), bp.div_pairs));
+        const int ow0 = (it - rest * pairs) * 2;
+        const int pl = first ? pl0
+                     : bp.whole ? static_cast<int>(fdiv(static_cast<uint32_t>(rest), bp.div_strips))
+                                : 0;
+        const int st = rest - pl * strips;
+        const int ohs = bb.oh0 + st * V;
+        const int nv = min(V, bb.oh1 - ohs);
+        const bool two = ow0 + 1 < g.Wo;
+        const float *xp = data + pl * HW;
+        const int iw0 = ow0 * SW_ - g.pw;
+        const int ih_s = ohs * SH_ - g.ph;
+        const int last_r = (nv - 1) * SH_ + 2;  // later rows only feed outputs past nv
+        bool cok[kCols];
+#pragma unroll
+        for (int j = 0; j < kCols; ++j)
+          cok[j] = static_cast<unsigned>(iw0 + j) < static_cast<unsigned>(g.W);
+        const int c = kOp == 0 ? (c0 + pl) % g.C : 0;
         float wr[9];
+        bool finite = true;
+        if (kOp == 0) {
 #pragma unroll
-        for (int k = 0; k < 9; ++k) wr[k] = wp[k];
-        const float b = bias ? __ldg(bias + (p0 + pl) % g.C) : 0.0f;
-        float *yp0 = y + (p0 + pl) * HoWo;
-        for (int r = t - pl * tpp; r < items_pp; r += tpp) {
-          const int oh = r / groups;
-          const int ow0 = (r - oh * groups) << 2;
-          constexpr int kCols = 3 * SW_ + 3;  // inputs under 4 adjacent outputs
-          float xr[3][kCols];
-          bool rok[3], cok[kCols];
-#pragma unroll
-          for (int kh = 0; kh < 3; ++kh) {
-            const int ih = oh * g.sh + kh - g.ph;
-            rok[kh] = static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
+          for (int k9 = 0; k9 < 9; ++k9) {
+            wr[k9] = first ? wnext[k9] : __ldg(w + c * 9 + k9);
+            finite = finite && isfinite(wr[k9]);
           }
-#pragma unroll
-          for (int j = 0; j < kCols; ++j) {
-            const int iw = ow0 * SW_ - g.pw + j;
-            cok[j] = static_cast<unsigned>(iw) < static_cast<unsigned>(g.W);
+        }
+        float *op = out + (pl * rows + st * V) * g.Wo + ow0;
+        if (kOp == 0 && !finite) {
+          // 0 * inf would differ from skipping the padded cell: exact path.
+          const float bv = bias ? __ldg(bias + c) : 0.0f;
+          for (int v = 0; v < nv; ++v) {
+            for (int cc = 0; cc < (two ? 2 : 1); ++cc) {
+              float o = window_out<0>(xp, w + c * 9, ohs + v, ow0 + cc, g, 0, bb.ih_lo);
+              if (bias) o += bv;
+              op[v * g.Wo + cc] = o;
+            }
           }
+          continue;
+        }
+        // Cells outside the plane (or past the strip's last row) read as the
+        // operation's identity -- 0 for sums (a running sum is never -0, and
+        // the weights are finite, so adding 0 * w changes nothing), -inf for
+        // the running max -- so every tap is combined unconditionally.
+        const float kPad = kOp == 1 ? -CUDART_INF_F : 0.0f;
+        float acc[V][2];
 #pragma unroll
-          for (int kh = 0; kh < 3; ++kh) {
-            const int ih = oh * g.sh + kh - g.ph;
+        for (int v = 0; v < V; ++v) acc[v][0] = acc[v][1] = kOp == 1 ? -CUDART_INF_F : 0.0f;
+        const float *xrow = xp + (ih_s - bb.ih_lo) * g.W + iw0;
 #pragma unroll
-            for (int j = 0; j < kCols; ++j)
-              xr[kh][j] = (rok[kh] && cok[j]) ? xp[ih * g.W + ow0 * SW_ - g.pw + j] : 0.0f;
-          }
-          float *yp = yp0 + oh * g.Wo;
+        for (int r = 0; r < kRows; ++r) {
+          const bool rok =
+              r <= last_r && static_cast<unsigned>(ih_s + r) < static_cast<unsigned>(g.H);
+          float xv[kCols];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ow = ow0 + q;
-            if (ow >= g.Wo) break;
-            float sum = 0.0f;
+          for (int j = 0; j < kCols; ++j) xv[j] = (rok && cok[j]) ? xrow[j] : kPad;
+          xrow += g.W;
 #pragma unroll
-            for (int kh = 0; kh < 3; ++kh) {
-              if (!rok[kh]) continue;
+          for (int v = 0; v < V; ++v) {
+            const int kh = r - v * SH_;
+            if (kh < 0 || kh > 2) continue;
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
               for (int kw = 0; kw < 3; ++kw) {
-                const int j = q * SW_ + kw;
-                if (cok[j]) sum += xr[kh][j] * wr[kh * 3 + kw];
+                const float xin = xv[cc * SW_ + kw];
+                if (kOp == 0)
+                  acc[v][cc] += xin * wr[kh * 3 + kw];
+                else if (kOp == 1)
+                  acc[v][cc] = (acc[v][cc] < xin) ? xin : acc[v][cc];  // std::max(m, v)
+                else
+                  acc[v][cc] += xin;
               }
             }
-            if (bias) sum += b;
-            yp[ow] = sum;
+          }
+        }
+        const float bv = (kOp == 0 && bias) ? __ldg(bias + c) : 0.0f;
+        int ncols[2] = {0, 0};
+        if (kOp == 2) {
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int kw = 0; kw < 3; ++kw) ncols[cc] += cok[cc * SW_ + kw] ? 1 : 0;
+        }
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+          if (v >= nv) break;
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            if (cc == 1 && !two) break;
+            float o = acc[v][cc];
+            if (kOp == 0 && bias) o += bv;
+            if (kOp == 2) {
+              const int ih0 = ih_s + v * SH_;
+              const int nrows = max(0, min(g.H, ih0 + 3) - max(0, ih0));
+              const int cnt = count_include_pad ? 9 : nrows * ncols[cc];
+              o = cnt > 0 ? o / static_cast<float>(cnt) : 0.0f;
+            }
+            op[v * g.Wo + cc] = o;
           }
         }
       }
     } else {
-    for (int it = t; it < cnt * items_pp; it += 256) {
-      const int pl = it / items_pp;
-      const int r = it - pl * items_pp;
-      const int oh = r / groups;
-      const int ow0 = (r - oh * groups) << 2;
-      const float *xp = sp + pl * HW;
-      const float *wp = sw + pl * taps;
-      float *yp = y + (p0 + pl) * HoWo + oh * g.Wo;
-      float b = 0.0f;
-      if (kOp == 0 && bias) b = __ldg(bias + (p0 + pl) % g.C);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int ow = ow0 + q;
-        if (ow < g.Wo) {
-          float v = window_out<kOp, KH_, KW_>(xp, wp, oh, ow, g, count_include_pad);
-          if (kOp == 0 && bias) v += b;
-          yp[ow] = v;
-        }
+      const int items = bb.cnt * rows * g.Wo;
+      for (int it = lane; it < items; it += 32) {
+        const int rest = static_cast<int>(fdiv(static_cast<uint32_t>(it), g.div_wo));
+        const int ow = it - rest * g.Wo;
+        const int pl = rest / rows;
+        const int r = rest - pl * rows;
+        const int c = kOp == 0 ? (c0 + pl) % g.C : 0;
+        float v = window_out<kOp>(data + pl * HW, w + static_cast<int64_t>(c) * taps, bb.oh0 + r,
+                                  ow, g, count_include_pad, bb.ih_lo);
+        if (kOp == 0 && bias) v += __ldg(bias + c);
+        out[(pl * rows + r) * g.Wo + ow] = v;
       }
     }
-    }
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
 }
 
 namespace {
 
-// Planes per batch for plane_window_kernel, 0 when a plane is too large.
-int plane_batch(const WindowGeom &g, int taps) {
-  const int64_t plane_bytes = (static_cast<int64_t>(g.H) * g.W + taps) * 4;
-  if (plane_bytes > kPlaneMaxBytes) return 0;
-  int np = static_cast<int>(kPlaneBatchBytes / plane_bytes);
-  if (np < 1) np = 1;
-  if (np > 64) np = 64;
-  return np;
+int64_t round4(int64_t v) { return (v + 3) & ~int64_t(3); }
+
+// Fraction of lane slots a batch of `items` fills when 32 lanes loop over it.
+double lane_fill(int64_t items) {
+  return static_cast<double>(items) / (32.0 * static_cast<double>(ceil_div(items, int64_t(32))));
 }
 
-template <int kOp>
-int launch_plane(cudaStream_t s, const float *x, const float *w, const float *bias, float *y,
-                 int64_t planes, const WindowGeom &g, int count_include_pad, int np) {
-  const int taps = g.KH * g.KW;
-  const size_t buf_floats =
-      (static_cast<size_t>(np) * (static_cast<size_t>(g.H) * g.W + (kOp == 0 ? taps : 0)) + 3) &
-      ~size_t(3);
-  const size_t smem = 2 * buf_floats * 4;  // double buffered
-  const int vec = ((g.H * g.W) % 4 == 0) && ((reinterpret_cast<uintptr_t>(x) & 15u) == 0);
-  int64_t blocks = ceil_div(planes, np);
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;
-  if (blocks > cap) blocks = cap;
-  const unsigned grid = static_cast<unsigned>(blocks);
-  bool done = false;
-  if constexpr (kOp == 0) {
-    if (g.KH == 3 && g.KW == 3 && g.sw == 1) {
-      if (int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(plane_window_kernel<0, 3, 3, 1>), static_cast<int>(smem))) return rc;
-      plane_window_kernel<0, 3, 3, 1><<<grid, 256, smem, s>>>(x, w, bias, y, planes, np, g,
-                                                             count_include_pad, vec);
-      done = true;
-    } else if (g.KH == 3 && g.KW == 3 && g.sw == 2) {
-      if (int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(plane_window_kernel<0, 3, 3, 2>), static_cast<int>(smem))) return rc;
-      plane_window_kernel<0, 3, 3, 2><<<grid, 256, smem, s>>>(x, w, bias, y, planes, np, g,
-                                                             count_include_pad, vec);
-      done = true;
+// Batches for band_window_kernel; false when the input rows under one output
+// row exceed a stage (the window_kernel family handles those).
+bool band_plan(const WindowGeom &g, int64_t planes, bool fast, BandPlan &bp) {
+  const int64_t HW = static_cast<int64_t>(g.H) * g.W;
+  const int V = !fast ? 1 : g.sh == 1 ? StripRows<1>::value : StripRows<2>::value;
+  const int64_t cols = fast ? (g.Wo + 1) / 2 : g.Wo;  // the 3x3 path pairs columns
+  const int64_t items_pp = static_cast<int64_t>((g.Ho + V - 1) / V) * cols;
+  const int64_t cap = (kBandStageBytes - 32) / 4;  // floats of input per stage
+  bp = BandPlan{};
+  if (HW <= cap) {
+    // As many planes as fit a stage and keep the batch at <= kBandItemsMax
+    // items, preferring a batch that fills the lanes.
+    int64_t np_max = cap / HW;
+    if (np_max > 64) np_max = 64;
+    int64_t np = 1;
+    double best = -1.0;
+    for (int64_t n = 1; n <= np_max; ++n) {
+      if (n > 1 && n * items_pp > kBandItemsMax) break;
+      const double f = lane_fill(n * items_pp);
+      if (f >= best - 1e-9) {
+        best = f;
+        np = n;
+      }
     }
-  }
-  if (done) {
-  } else if (g.KH == 3 && g.KW == 3) {
-    if (int rc = ensure_dynamic_smem(
-            reinterpret_cast<const void *>(plane_window_kernel<kOp, 3, 3, 0>), static_cast<int>(smem)))
-      return rc;
-    plane_window_kernel<kOp, 3, 3, 0><<<grid, 256, smem, s>>>(x, w, bias, y, planes, np, g,
-                                                             count_include_pad, vec);
+    bp.whole = 1;
+    bp.np = static_cast<int>(np);
+    bp.R = g.Ho;
+    bp.bands = 1;
+    bp.batches = ceil_div(planes, np);
+    bp.strips = (g.Ho + V - 1) / V;
   } else {
-    if (int rc = ensure_dynamic_smem(
-            reinterpret_cast<const void *>(plane_window_kernel<kOp, 0, 0, 0>), static_cast<int>(smem)))
-      return rc;
-    plane_window_kernel<kOp, 0, 0, 0><<<grid, 256, smem, s>>>(x, w, bias, y, planes, np, g,
-                                                             count_include_pad, vec);
+    auto rows_in = [&](int64_t R) {
+      const int64_t r = (R - 1) * g.sh + g.KH;
+      return r < g.H ? r : static_cast<int64_t>(g.H);
+    };
+    if (rows_in(1) * g.W > cap) return false;
+    int64_t R = 1;
+    while (R < g.Ho && rows_in(R + 1) * g.W <= cap &&
+           ceil_div(R + 1, static_cast<int64_t>(V)) * cols <= kBandItemsMax)
+      ++R;
+    if (fast && R > V) R -= R % V;
+    bp.whole = 0;
+    bp.np = 1;
+    bp.R = static_cast<int>(R);
+    bp.bands = static_cast<int>(ceil_div(static_cast<int64_t>(g.Ho), R));
+    bp.batches = planes * bp.bands;
   }
+  bp.stage_floats = static_cast<int>(round4(cap + 8));
+  bp.div_pairs = make_fastdiv(static_cast<uint32_t>((g.Wo + 1) / 2));
+  bp.div_strips = make_fastdiv(static_cast<uint32_t>(bp.strips > 0 ? bp.strips : 1));
+  return true;
+}
+
+template <int kOp, int SH_, int SW_>
+int launch_band_kernel(cudaStream_t s, const float *x, const float *w, const float *bias,
+                       float *y, int64_t planes, const BandPlan &bp, const WindowGeom &g,
+                       int count_include_pad) {
+  auto kernel = band_window_kernel<kOp, SH_, SW_>;
+  const size_t smem =
+      static_cast<size_t>(kBandStages) * bp.stage_floats * 4 + 2 * kBandStages * 8 + 16;
+  if (int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), static_cast<int>(smem)))
+    return rc;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kBandThreads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  int64_t blocks = static_cast<int64_t>(sm_count()) * per_sm;
+  if (blocks > bp.batches) blocks = bp.batches;
+  kernel<<<static_cast<unsigned>(blocks), kBandThreads, smem, s>>>(
+      x, w, bias, y, planes, bp, g, count_include_pad, device_status_word());
   count_launch();
   return launch_result();
+}
+
+// Runs window operation kOp through band_window_kernel; returns 1 when the
+// geometry has no staging plan (the caller then uses the window_kernel
+// family).
+template <int kOp>
+int launch_band(cudaStream_t s, const float *x, const float *w, const float *bias, float *y,
+                int64_t planes, const WindowGeom &g, int count_include_pad) {
+  if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(y) & 3u)) return 1;
+  const bool fast = g.KH == 3 && g.KW == 3 && g.sh == g.sw && (g.sh == 1 || g.sh == 2);
+  BandPlan bp;
+  if (!band_plan(g, planes, fast, bp)) return 1;
+  if (fast && g.sh == 1)
+    return launch_band_kernel<kOp, 1, 1>(s, x, w, bias, y, planes, bp, g, count_include_pad);
+  if (fast)
+    return launch_band_kernel<kOp, 2, 2>(s, x, w, bias, y, planes, bp, g, count_include_pad);
+  return launch_band_kernel<kOp, 0, 0>(s, x, w, bias, y, planes, bp, g, count_include_pad);
 }
 
 }  // namespace
@@ -426,8 +610,8 @@ extern "C" int nplk_depthwise_conv2d(void *stream, const nplk_conv_geom_t *g, co
   wg.div_ho = make_fastdiv(static_cast<uint32_t>(wg.Ho));
   wg.div_c = make_fastdiv(static_cast<uint32_t>(wg.C));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int np = plane_batch(wg, wg.KH * wg.KW);
-  if (np > 0) return launch_plane<0>(s, x, w, bias, out, g->n * g->c_in, wg, 0, np);
+  const int rc = launch_band<0>(s, x, w, bias, out, g->n * g->c_in, wg, 0);
+  if (rc != 1) return rc;
   dwconv_kernel<<<window_grid(total), 256, 0, s>>>(x, w, bias, out,
                                                    static_cast<uint32_t>(total), wg);
   count_launch();
@@ -460,12 +644,10 @@ extern "C" int nplk_pool2d(void *stream, int64_t n, int64_t c, int64_t h, int64_
   wg.div_ho = make_fastdiv(static_cast<uint32_t>(wg.Ho));
   wg.div_c = make_fastdiv(static_cast<uint32_t>(wg.C));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int np = plane_batch(wg, 0);
-  if (np > 0)
-    return pool_type == 0 ? launch_plane<1>(s, x, nullptr, nullptr, y, n * c, wg,
-                                            count_include_pad, np)
-                          : launch_plane<2>(s, x, nullptr, nullptr, y, n * c, wg,
-                                            count_include_pad, np);
+  const int rc = pool_type == 0
+                     ? launch_band<1>(s, x, nullptr, nullptr, y, n * c, wg, count_include_pad)
+                     : launch_band<2>(s, x, nullptr, nullptr, y, n * c, wg, count_include_pad);
+  if (rc != 1) return rc;
   if (pool_type == 0)
     pool_kernel<0><<<window_grid(total), 256, 0, s>>>(x, y, static_cast<uint32_t>(total), wg,
                                                       count_include_pad);
