@@ -3,9 +3,13 @@
 //
 // GEMM view: D[m][co] = sum_k A[m][k] * W'[co][k]
 //   m  = (n, oh, ow)           output pixel, M = N*Ho*Wo
-//   k  = (ci, kh, kw) in one of two orders, K = KH*KW*Cin:
+//   k  = (ci, kh, kw) in one of three orders, K = KH*KW*Cin:
 //        Cin % 32 == 0: channel-block-major, k = ((cb*KH*KW) + tap)*32 + ci%32,
 //                       so each 32-wide k-block is one tap over 32 channels;
+//        filter rows of 3..8 columns (no column dilation): row order,
+//                       k = (ci*KH + kh)*S + kw with S = 4 or 8 slots per
+//                       filter row (slots past KW hold zero), so a thread
+//                       reads S contiguous input columns per filter row;
 //        otherwise:     tap-major, k = tap*Cin + ci
 //   A[m][k] = x[n][ci][oh*sh - pt + kh*dh][ow*sw - pl + kw*dw]  (0 outside)
 //   W'[co][k] = w[co][ci][kh][kw]
@@ -59,10 +63,24 @@ struct ConvTraits {
       1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20;  // + epilogue constants
 };
 
-// kFastC: C is a multiple of 32, so every 32-wide k-block is one filter tap
-// across 32 consecutive channels (k ordered channel-block-major, see
-// conv_prep_kernel) and the gather needs no per-element tap bookkeeping.
-template <int BNC, bool kFastC, int kAct>
+// k orders of the direct kernel (4 and 8 are the row order's slot counts).
+constexpr int kModeTaps = 0;
+constexpr int kModeChannelBlocks = 1;
+
+// Row-order slots per filter row for a geometry, 0 when the row order does not
+// apply: channels not a multiple of 32 (channel blocks take those), filter
+// rows of 3..8 columns, no column dilation.
+inline int conv_row_slots(int64_t C, int64_t KW, int64_t dw) {
+  if (C % kConvBK == 0 || dw != 1 || KW < 3 || KW > 8) return 0;
+  return KW <= 4 ? 4 : 8;
+}
+
+// kMode (the k order, see conv_prep_kernel): kModeChannelBlocks -- C is a
+// multiple of 32, so every 32-wide k-block is one filter tap across 32
+// consecutive channels and the gather needs no per-element tap bookkeeping;
+// 4 or 8 -- row order with that many slots per filter row; kModeTaps --
+// tap-major, any geometry.
+template <int BNC, int kMode, int kAct>
 __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
   using T = ConvTraits<BNC>;
@@ -118,6 +136,7 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     const int items = my_tiles * p.k_blocks;
     int cur_tile = -1;
     int ih0[2] = {0, 0}, iw0[2] = {0, 0};
+    uint32_t cmask[2] = {0u, 0u};  // row order: filter columns inside the image
     bool valid[2] = {false, false};
     const float *xb[2] = {p.x, p.x};
     int nb = 0;
@@ -145,11 +164,44 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
           ih0[r] = oh * p.sh - p.pt;
           iw0[r] = ow * p.sw - p.pl;
           xb[r] = p.x + static_cast<int64_t>(n) * p.CHW;
+          if (kMode == 4 || kMode == 8) {
+            cmask[r] = 0u;
+            for (int kw = 0; kw < p.KW; ++kw)
+              if (static_cast<unsigned>(iw0[r] + kw) < static_cast<unsigned>(p.W))
+                cmask[r] |= 1u << kw;
+          }
         }
       }
       // Gather 2 rows x 32 k into registers before waiting for the stage.
       float v[2][32];
-      if (kFastC) {
+      if (kMode == 4 || kMode == 8) {
+        // Row order: the k-block holds 32 / S (channel, filter row) pairs of
+        // S filter columns; each pair is S contiguous input columns.
+        constexpr int S = kMode == 8 ? 8 : 4;
+        constexpr int kPairs = kConvBK / S;
+        const int q0 = kb * kPairs;
+        int ci = q0 / p.KH;
+        int kh = q0 - ci * p.KH;
+#pragma unroll
+        for (int i = 0; i < kPairs; ++i) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int ih = ih0[r] + kh * p.dh;
+            const uint32_t m = (ci < p.C && valid[r] &&
+                                static_cast<unsigned>(ih) < static_cast<unsigned>(p.H))
+                                   ? cmask[r]
+                                   : 0u;
+            const float *base = xb[r] + static_cast<int64_t>(ci) * p.HW +
+                                static_cast<int64_t>(ih) * p.W + iw0[r];
+#pragma unroll
+            for (int kw = 0; kw < S; ++kw) v[r][i * S + kw] = ((m >> kw) & 1u) ? __ldg(base + kw) : 0.0f;
+          }
+          if (++kh == p.KH) {
+            kh = 0;
+            ++ci;
+          }
+        }
+      } else if (kMode == kModeChannelBlocks) {
         const int taps = p.KH * p.KW;
         const int cb = kb / taps;
         const int tap = kb - cb * taps;
@@ -310,10 +362,11 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
   }
 }
 
-// Weight preparation: w[co][ci][kh][kw] -> tap-major, tf32-split, blocked
-// [n_blocks][2][BNC][kp] (zero padded), plus the epilogue constants.
+// Weight preparation: w[co][ci][kh][kw] -> the k order of the geometry
+// (channel blocks, row order with row_slots > 0, else tap-major), tf32-split,
+// blocked [n_blocks][2][BNC][kp] (zero padded), plus the epilogue constants.
 __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, int KH, int KW,
-                                 int kp, int bnc, float *__restrict__ wsplit,
+                                 int row_slots, int kp, int bnc, float *__restrict__ wsplit,
                                  int64_t wsplit_elems, const float *bias, const float *mean,
                                  const float *var, const float *gamma, const float *beta,
                                  float eps, float *__restrict__ ep, int cout_pad) {
@@ -327,7 +380,15 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
     const int k = static_cast<int>(i - rowg * kp);
     const int co = static_cast<int>(rowg);
     float x = 0.0f;
-    if (co < Cout && k < K) {
+    if (row_slots > 0) {
+      // row order: k = (ci*KH + kh)*row_slots + kw, slots past KW zero
+      const int q = k / row_slots;
+      const int kw = k - q * row_slots;
+      const int ci = q / KH;
+      const int kh = q - ci * KH;
+      if (co < Cout && ci < C && kw < KW)
+        x = w[((static_cast<int64_t>(co) * C + ci) * KH + kh) * KW + kw];
+    } else if (co < Cout && k < K) {
       int ci, tap;
       if (C % kConvBK == 0) {
         // channel-block-major: k = ((cb * KH*KW) + tap) * 32 + ci_in
@@ -379,6 +440,7 @@ enum ConvPath {
 // the NHWC input planes: x_hi and x_lo (im2col path) or raw x (window path).
 struct ConvPlan {
   int bnc;
+  int mode;  // k order of the direct kernel: kModeTaps, kModeChannelBlocks, 4 or 8
   int64_t kp, n_blocks, cout_pad;
   size_t w_bytes, ep_bytes;
   int path;
@@ -426,7 +488,9 @@ ConvParams conv_params(const nplk_conv_geom_t *g, const ConvPlan &c) {
 ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
   ConvPlan c{};
   c.bnc = g->c_out <= 64 ? 64 : 128;
-  const int64_t K = g->c_in * g->kh * g->kw;
+  const int slots = conv_row_slots(g->c_in, g->kw, g->dil_w);
+  c.mode = g->c_in % kConvBK == 0 ? kModeChannelBlocks : slots > 0 ? slots : kModeTaps;
+  const int64_t K = slots > 0 ? g->c_in * g->kh * slots : g->c_in * g->kh * g->kw;
   c.kp = ceil_div(K, kConvBK) * kConvBK;
   c.n_blocks = ceil_div(g->c_out, c.bnc);
   c.cout_pad = c.n_blocks * c.bnc;
@@ -465,7 +529,7 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
   return c;
 }
 
-template <int BNC, bool kFastC, int kAct>
+template <int BNC, int kMode, int kAct>
 int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
   using T = ConvTraits<BNC>;
   CUtensorMap map_w;
@@ -473,29 +537,38 @@ int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvPara
                                     kConvBK, 2 * BNC);
   if (rc) return rc;
   rc = ensure_dynamic_smem(
-      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kFastC, kAct>), T::kSmemBytes);
+      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kMode, kAct>), T::kSmemBytes);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_igemm_3xtf32_kernel<BNC, kFastC, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm);
+  conv_igemm_3xtf32_kernel<BNC, kMode, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm);
   count_launch();
   return launch_result();
 }
 
-template <int BNC, bool kFastC>
+template <int BNC, int kMode>
 int dispatch_act(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
-  if (prm.act == 0) return launch_conv<BNC, kFastC, kEpiActNone>(s, c, wsplit, prm);
-  if (prm.act == 1) return launch_conv<BNC, kFastC, kEpiActRelu>(s, c, wsplit, prm);
-  return launch_conv<BNC, kFastC, kEpiActAny>(s, c, wsplit, prm);
+  if (prm.act == 0) return launch_conv<BNC, kMode, kEpiActNone>(s, c, wsplit, prm);
+  if (prm.act == 1) return launch_conv<BNC, kMode, kEpiActRelu>(s, c, wsplit, prm);
+  return launch_conv<BNC, kMode, kEpiActAny>(s, c, wsplit, prm);
 }
 
-int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm,
-                  bool fast) {
-  if (c.bnc == 64)
-    return fast ? dispatch_act<64, true>(s, c, wsplit, prm)
-                : dispatch_act<64, false>(s, c, wsplit, prm);
-  return fast ? dispatch_act<128, true>(s, c, wsplit, prm)
-              : dispatch_act<128, false>(s, c, wsplit, prm);
+template <int BNC>
+int dispatch_mode(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
+  switch (c.mode) {
+    case kModeChannelBlocks:
+      return dispatch_act<BNC, kModeChannelBlocks>(s, c, wsplit, prm);
+    case 4:
+      return dispatch_act<BNC, 4>(s, c, wsplit, prm);
+    case 8:
+      return dispatch_act<BNC, 8>(s, c, wsplit, prm);
+    default:
+      return dispatch_act<BNC, kModeTaps>(s, c, wsplit, prm);
+  }
+}
+
+int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
+  return c.bnc == 64 ? dispatch_mode<64>(s, c, wsplit, prm) : dispatch_mode<128>(s, c, wsplit, prm);
 }
 
 }  // namespace
@@ -569,7 +642,8 @@ extern "C" int nplk_conv2d_prepare(void *stream, const nplk_conv_geom_t *g, cons
   if (blocks > 4096) blocks = 4096;
   conv_prep_kernel<<<static_cast<unsigned>(blocks), threads, 0, s>>>(
       w, static_cast<int>(g->c_out), static_cast<int>(g->c_in), static_cast<int>(g->kh),
-      static_cast<int>(g->kw), static_cast<int>(c.kp), c.bnc, wsplit, wsplit_elems, bias,
+      static_cast<int>(g->kw), c.mode == 4 || c.mode == 8 ? c.mode : 0, static_cast<int>(c.kp),
+      c.bnc, wsplit, wsplit_elems, bias,
       bn_mean, bn_var, bn_gamma, bn_beta, bn_eps, ep, static_cast<int>(c.cout_pad));
   count_launch();
   return launch_result();
@@ -639,7 +713,7 @@ int run_plan(cudaStream_t s, const nplk_conv_geom_t *g, const float *x, const Co
     }
     case kPathDirect:
       prm.x = x;
-      return dispatch_conv(s, c, wsplit, prm, g->c_in % kConvBK == 0);
+      return dispatch_conv(s, c, wsplit, prm);
     default:
       return kErrUnsupported;
   }

@@ -124,6 +124,9 @@ def test_stem_conv_bn_relu_then_maxpool():
     (2, 8, 16, 16, 12, (3, 3), (1, 1), (2, 2), (2, 2)),     # dilation 2
     (1, 100, 7, 7, 96, (3, 3), (1, 1), (1, 1), (1, 1)),     # K = 900, not a multiple of 32
     (5, 3, 31, 33, 64, (7, 7), (2, 2), (3, 3), (1, 1)),     # tiles straddle images
+    (1, 12, 15, 16, 33, (4, 4), (2, 2), (1, 1), (1, 1)),    # row order, 4 slots all used
+    (2, 7, 19, 23, 40, (2, 6), (1, 2), (0, 2), (1, 1)),     # row order, 8 slots, KH != KW
+    (2, 6, 20, 18, 16, (3, 5), (1, 1), (2, 2), (2, 1)),     # row order with vertical dilation
 ])
 def test_conv2d_shapes(n, cin, h, w, cout, k, stride, pad, dil):
     lib = S.gpu_lib()
