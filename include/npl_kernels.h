@@ -48,10 +48,20 @@ extern "C" {
 
 /* GEMM flags. */
 #define NPLK_GEMM_TF32_FAST 1u /* one TF32 pass instead of three (reported separately) */
+/* Operand form of nplk_gemm. With a workspace of nplk_gemm_workspace_size()
+ * bytes, A and B are first split into tf32 hi/lo copies there (the faster
+ * form). Without one (NULL or too small), A and B are read in place (raw form:
+ * the tensor core truncates them to tf32, the lo parts are formed in shared
+ * memory), which needs A, B 16-byte aligned and lda, ldb multiples of 4.
+ * These flags force one form (RAW fails with NPL_ERR_UNSUPPORTED when A or B
+ * do not qualify). */
+#define NPLK_GEMM_SPLIT_OPERANDS 2u
+#define NPLK_GEMM_RAW_OPERANDS 4u
 
 /* ---- dense contractions (tcgen05, 3xTF32) ---------------------------------- */
 
-/* Scratch bytes nplk_gemm needs for an M x N x K product (hi/lo operand splits). */
+/* Scratch bytes nplk_gemm needs for an M x N x K product (hi/lo operand splits;
+ * the raw operand form uses none, so the workspace may then be NULL). */
 NPL_API size_t nplk_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 
 /* C[M,N] = act(alpha * A[M,K] @ B[K,N] + beta * C + bias[N]), fp32 row-major

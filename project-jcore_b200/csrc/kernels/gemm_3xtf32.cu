@@ -19,6 +19,7 @@
 //   4. warps 2-5 drain the (double-buffered) accumulator: C = alpha*(D[:, :BN]
 //      + D[:, BN:]) + beta*C + bias, activation, store.
 #include <cuda_runtime.h>
+#include <math_constants.h>
 
 #include "nplk_device.cuh"
 #include "nplk_host.h"
@@ -67,6 +68,70 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_b
   const int local = tile - group * per_group;
   mb = first_m + local % gsize;
   nb = local / gsize;
+}
+
+// Drains one accumulator tile row (this thread's row r of the tile) from
+// TMEM: C = alpha*(D[:, :BN] + D[:, BN:]) + beta*C + bias, activation, store.
+template <int BN>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t t_row, int r,
+                                                   int nb, bool vec_ok) {
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t v[32], w[32];
+    tmem_ld32(t_row + c0, v);
+    if (!p.one_pass) {
+      tmem_ld32(t_row + BN + c0, w);
+      tmem_wait_ld2(v, w);
+    } else {
+      tmem_wait_ld(v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) w[j] = 0u;
+    }
+    const int col0 = nb * BN + c0;
+    if (r < p.M && col0 < p.N) {
+      float *crow = p.C + static_cast<int64_t>(r) * p.ldc;
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        out[j] = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
+      if (vec_ok && col0 + 32 <= p.N) {
+        float4 *dst = reinterpret_cast<float4 *>(crow + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 o = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+          if (p.beta != 0.0f) {
+            const float4 c = dst[q];
+            o.x += p.beta * c.x;
+            o.y += p.beta * c.y;
+            o.z += p.beta * c.z;
+            o.w += p.beta * c.w;
+          }
+          if (p.bias) {
+            o.x += p.bias[col0 + 4 * q];
+            o.y += p.bias[col0 + 4 * q + 1];
+            o.z += p.bias[col0 + 4 * q + 2];
+            o.w += p.bias[col0 + 4 * q + 3];
+          }
+          o.x = apply_act(o.x, p.act, p.act_alpha);
+          o.y = apply_act(o.y, p.act, p.act_alpha);
+          o.z = apply_act(o.z, p.act, p.act_alpha);
+          o.w = apply_act(o.w, p.act, p.act_alpha);
+          dst[q] = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = col0 + j;
+          if (col < p.N) {
+            float o = out[j];
+            if (p.beta != 0.0f) o += p.beta * crow[col];
+            if (p.bias) o += p.bias[col];
+            crow[col] = apply_act(o, p.act, p.act_alpha);
+          }
+        }
+      }
+    }
+  }
 }
 
 template <int BN>
@@ -208,66 +273,249 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t v[32], w[32];
-        tmem_ld32(t_row + c0, v);
-        if (!p.one_pass) {
-          tmem_ld32(t_row + BN + c0, w);
-          tmem_wait_ld2(v, w);
-        } else {
-          tmem_wait_ld(v);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = 0u;
-        }
-        const int col0 = nb * BN + c0;
-        if (r < p.M && col0 < p.N) {
-          float *crow = p.C + static_cast<int64_t>(r) * p.ldc;
-          float out[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            out[j] = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
-          if (vec_ok && col0 + 32 <= p.N) {
-            float4 *dst = reinterpret_cast<float4 *>(crow + col0);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 o = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-              if (p.beta != 0.0f) {
-                const float4 c = dst[q];
-                o.x += p.beta * c.x;
-                o.y += p.beta * c.y;
-                o.z += p.beta * c.z;
-                o.w += p.beta * c.w;
-              }
-              if (p.bias) {
-                o.x += p.bias[col0 + 4 * q];
-                o.y += p.bias[col0 + 4 * q + 1];
-                o.z += p.bias[col0 + 4 * q + 2];
-                o.w += p.bias[col0 + 4 * q + 3];
-              }
-              o.x = apply_act(o.x, p.act, p.act_alpha);
-              o.y = apply_act(o.y, p.act, p.act_alpha);
-              o.z = apply_act(o.z, p.act, p.act_alpha);
-              o.w = apply_act(o.w, p.act, p.act_alpha);
-              dst[q] = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = col0 + j;
-              if (col < p.N) {
-                float o = out[j];
-                if (p.beta != 0.0f) o += p.beta * crow[col];
-                if (p.bias) o += p.bias[col];
-                crow[col] = apply_act(o, p.act, p.act_alpha);
-              }
-            }
-          }
-        }
-      }
+gemm_epilogue_tile<BN>(p, t_row, r, nb, vec_ok);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, T::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Raw-operand form: A (row-major [M][K], a K-major operand) and B (row-major
+// [K][N], read as an MN-major operand) are loaded as they are by TMA; the
+// tensor core truncates them to tf32 for the hi parts, and converter warps
+// form the lo parts (x - trunc(x), 0 for +-inf) in shared memory next to
+// them. No split kernels and no workspace; half the operand bytes of the
+// split form cross L2 per tile, but forming lo costs shared-memory bandwidth,
+// which bounds this GEMM, so the split form stays the default when a
+// workspace is given.
+//   warp 0      TMA producer: A box [128 rows][32 K] (128-byte swizzle), B
+//               boxes [32 K][32 N] (128-byte swizzle of 32-byte atoms, the
+//               layout MN-major tf32 operands need);
+//   warp 1      MMA issuer:   MMA(A_raw, [B_raw | B_lo]) N = 2*BN, then
+//                             MMA(A_lo, B_raw) N = BN;
+//   warps 2-5   epilogue (gemm_epilogue_tile);
+//   warps 6-9   converters: A_lo and B_lo, elementwise over the swizzled tiles
+//               (raw and lo tiles share one layout, so no swizzle arithmetic).
+// ---------------------------------------------------------------------------
+constexpr int kRawConvWarps = 4;
+constexpr int kRawThreads = kGemmThreads + kRawConvWarps * 32;
+
+template <int BN>
+struct RawGemmTraits {
+  static constexpr int kStages = BN == 128 ? 3 : 4;
+  static constexpr int kAHalf = kGemmBM * kGemmBK * 4;  // one A tile, 16 KB
+  static constexpr int kBAtom = 32 * kGemmBK * 4;       // [32 K][32 N] B atom, 4 KB
+  static constexpr int kBHalf = (BN / 32) * kBAtom;     // one B tile
+  // Stage: A_raw, A_lo, B_raw atoms, B_lo atoms (1024-byte aligned pieces).
+  static constexpr int kStageBytes = 2 * kAHalf + 2 * kBHalf;
+  static constexpr int kTxBytes = kAHalf + kBHalf;  // what TMA writes per stage
+  static constexpr int kAccCols = 2 * BN;
+  static constexpr int kTmemCols = 2 * kAccCols;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+};
+
+__device__ __forceinline__ float tf32_lo_trunc(float x) {
+  const float hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  return fabsf(x) == CUDART_INF_F ? 0.0f : x - hi;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kRawThreads, 1)
+    gemm_3xtf32_raw_kernel(const __grid_constant__ CUtensorMap map_a,
+                           const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+  using T = RawGemmTraits<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + T::kStages * T::kStageBytes);
+  uint64_t *lo_ready = full + T::kStages;
+  uint64_t *empty = lo_ready + T::kStages;
+  uint64_t *acc_full = empty + T::kStages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&lo_ready[s], kRawConvWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, T::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.m_blocks * p.n_blocks;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pending = 0;  // stages that received a copy, with its phase
+      uint32_t pending_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
+                         kStatusTimeoutProducer))
+            goto producer_done;
+          uint8_t *st = smem + stage * T::kStageBytes;
+          mbar_arrive_expect_tx(&full[stage], T::kTxBytes);
+          tma_load_2d(&map_a, &full[stage], st, kb * kGemmBK, mb * kGemmBM);
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j)
+            tma_load_2d(&map_b, &full[stage], st + 2 * T::kAHalf + j * T::kBAtom,
+                        nb * BN + 32 * j, kb * kGemmBK);
+          pending |= 1u << stage;
+          pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == T::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // Let the last copy into each stage land before the CTA can exit (they
+      // already have unless the CTA aborted).
+      for (int s2 = 0; s2 < T::kStages; ++s2)
+        if ((pending >> s2) & 1u) mbar_drain(&full[s2], (pending_phase >> s2) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_2n = umma_idesc_tf32(kGemmBM, 2 * BN) | kUmmaIdescBMajorMN;
+      const uint32_t idesc_n = umma_idesc_tf32(kGemmBM, BN) | kUmmaIdescBMajorMN;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
+                       kStatusTimeoutAccFree))
+          break;
+        tc_fence_after_sync();
+        const uint32_t d_tmem = tmem_base + acc * T::kAccCols;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&lo_ready[stage], phase, abort_flag, p.status, kStatusTimeoutMma))
+            goto mma_done;
+          tc_fence_after_sync();
+          const uint32_t st = smem_u32(smem + stage * T::kStageBytes);
+          // A (K-major): a K = 8 step is 32 bytes (+2 in the address field).
+          // B (MN-major, 32-byte-atom swizzle): a K = 8 step is 8 rows of
+          // 128 bytes (+64); the B_lo atoms follow the B_raw atoms at the same
+          // 4 KB stride, so one descriptor with N = 2*BN covers [B_raw | B_lo].
+          const uint64_t a_raw = umma_desc_sw128(st);
+          const uint64_t a_lo = umma_desc_sw128(st + T::kAHalf);
+          const uint64_t b = umma_desc_mn_sw128_32b(st + 2 * T::kAHalf, T::kBAtom);
+          if (p.one_pass) {
+#pragma unroll
+            for (int kk = 0; kk < kGemmBK / 8; ++kk)
+              mma_tf32_ss(d_tmem, a_raw + 2 * kk, b + 64 * kk, idesc_n,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kGemmBK / 8; ++kk) {
+              mma_tf32_ss(d_tmem, a_raw + 2 * kk, b + 64 * kk, idesc_2n,
+                          (kb > 0 || kk > 0) ? 1u : 0u);
+              mma_tf32_ss(d_tmem, a_lo + 2 * kk, b + 64 * kk, idesc_n, 1u);
+            }
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == T::kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        mma_commit(&acc_full[acc]);
+      }
+    mma_done:;
+    }
+  } else if (warp < 6) {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
+                        ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after_sync();
+      int mb, nb;
+      gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(acc * T::kAccCols);
+      gemm_epilogue_tile<BN>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok);
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  } else {
+    // ---------------- converters (warps 6..9) ----------------
+    const int ct = threadIdx.x - 6 * 32;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    const int items = (num_tiles > static_cast<int>(blockIdx.x)
+                           ? (num_tiles - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1
+                           : 0) *
+                      p.k_blocks;
+    for (int it = 0; it < items; ++it) {
+      if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutStage)) break;
+      uint8_t *st = smem + stage * T::kStageBytes;
+      if (!p.one_pass) {
+        const float4 *a4 = reinterpret_cast<const float4 *>(st);
+        float4 *al4 = reinterpret_cast<float4 *>(st + T::kAHalf);
+#pragma unroll 4
+        for (int i = ct; i < T::kAHalf / 16; i += kRawConvWarps * 32) {
+          const float4 v = a4[i];
+          al4[i] = make_float4(tf32_lo_trunc(v.x), tf32_lo_trunc(v.y), tf32_lo_trunc(v.z),
+                               tf32_lo_trunc(v.w));
+        }
+        const float4 *b4 = reinterpret_cast<const float4 *>(st + 2 * T::kAHalf);
+        float4 *bl4 = reinterpret_cast<float4 *>(st + 2 * T::kAHalf + T::kBHalf);
+#pragma unroll 4
+        for (int i = ct; i < T::kBHalf / 16; i += kRawConvWarps * 32) {
+          const float4 v = b4[i];
+          bl4[i] = make_float4(tf32_lo_trunc(v.x), tf32_lo_trunc(v.y), tf32_lo_trunc(v.z),
+                               tf32_lo_trunc(v.w));
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&lo_ready[stage]);
+      if (++stage == T::kStages) {
+        stage = 0;
+        phase ^= 1u;
+      }
     }
   }
 
@@ -321,6 +569,33 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
                              T::kSmemBytes, stream, map_a, map_b, prm);
 }
 
+// The raw-operand form applies when TMA can read A and B in place: 16-byte
+// aligned bases and row pitches, and rows of at least 16 bytes.
+bool gemm_raw_ok(const float *A, int64_t lda, const float *B, int64_t ldb, int64_t N,
+                 int64_t K) {
+  return (reinterpret_cast<uintptr_t>(A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0 &&
+         lda % 4 == 0 && ldb % 4 == 0 && K >= 4 && N >= 4;
+}
+
+template <int BN>
+int launch_gemm_raw(cudaStream_t stream, const GemmPlan &g, const float *A, int64_t lda,
+                    const float *B, int64_t ldb, GemmParams prm) {
+  using T = RawGemmTraits<BN>;
+  CUtensorMap map_a, map_b;
+  int rc = encode_tmap_2d_f32_sw128(&map_a, A, prm.K, prm.M, lda * 4, kGemmBK, kGemmBM);
+  if (rc) return rc;
+  rc = encode_tmap_2d_f32_sw128_atom32(&map_b, B, prm.N, prm.K, ldb * 4, 32, kGemmBK);
+  if (rc) return rc;
+  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN>),
+                           T::kSmemBytes);
+  if (rc) return rc;
+  const int64_t tiles = g.m_blocks * g.n_blocks;
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  gemm_3xtf32_raw_kernel<BN><<<grid, kRawThreads, T::kSmemBytes, stream>>>(map_a, map_b, prm);
+  count_launch();
+  return launch_result();
+}
+
 }  // namespace
 
 // Split launchers (split_tf32.cu).
@@ -351,21 +626,9 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
     return kErrUnsupported;
   const GemmPlan g = plan_gemm(M, N, K);
-  if (!workspace || workspace_bytes < g.a_bytes + g.b_bytes) return kErrInvalidArg;
-  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kErrInvalidArg;
   if (!status) status = device_status_word();
   if (!status) return kErrInternal;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  float *a_split = static_cast<float *>(workspace);
-  float *b_split = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + g.a_bytes);
-
-  int rc = launch_split_rows(s, A, M, K, lda, 0, a_split, kGemmBM, g.kp, g.m_blocks * kGemmBM);
-  if (rc) return rc;
-  // The B split overlaps the A split and the GEMM kernel's set-up overlaps
-  // both (programmatic dependent launch); the GEMM's TMA producer waits for
-  // the splits before its first load.
-  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn, true);
-  if (rc) return rc;
 
   GemmParams prm{};
   prm.M = static_cast<int>(M);
@@ -383,6 +646,35 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
   prm.act_alpha = act_alpha;
   prm.one_pass = (flags & NPLK_GEMM_TF32_FAST) ? 1 : 0;
   prm.status = status;
+
+  // Operand form: split (hi/lo copies in the workspace, then the GEMM) when
+  // the workspace suffices -- it is the faster form: the GEMM is bound by
+  // shared-memory bandwidth, and forming the lo parts in shared memory adds
+  // ~22% to it (8192x4096x16384: 236.7 vs 194.8 TFLOP/s; 1024^3: 37.3 vs
+  // 36.5 us with the split kernels included) -- else raw (A and B read in
+  // place, no workspace) when TMA can read them. Callers may force either.
+  const bool raw_ok = gemm_raw_ok(A, lda, B, ldb, N, K);
+  const bool have_ws = workspace && workspace_bytes >= g.a_bytes + g.b_bytes;
+  if ((flags & NPLK_GEMM_RAW_OPERANDS) && !raw_ok) return kErrUnsupported;
+  const bool raw = (flags & NPLK_GEMM_RAW_OPERANDS) ||
+                   (!have_ws && raw_ok && !(flags & NPLK_GEMM_SPLIT_OPERANDS));
+  if (raw) {
+    if (g.bn == 128) return launch_gemm_raw<128>(s, g, A, lda, B, ldb, prm);
+    return launch_gemm_raw<64>(s, g, A, lda, B, ldb, prm);
+  }
+
+  if (!workspace || workspace_bytes < g.a_bytes + g.b_bytes) return kErrInvalidArg;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kErrInvalidArg;
+  float *a_split = static_cast<float *>(workspace);
+  float *b_split = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + g.a_bytes);
+
+  int rc = launch_split_rows(s, A, M, K, lda, 0, a_split, kGemmBM, g.kp, g.m_blocks * kGemmBM);
+  if (rc) return rc;
+  // The B split overlaps the A split and the GEMM kernel's set-up overlaps
+  // both (programmatic dependent launch); the GEMM's TMA producer waits for
+  // the splits before its first load.
+  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn, true);
+  if (rc) return rc;
   if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm);
   return launch_gemm<64>(s, g, a_split, b_split, prm);
 }

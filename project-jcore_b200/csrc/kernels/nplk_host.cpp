@@ -109,9 +109,30 @@ int ensure_dynamic_smem(const void *func, int bytes) {
   return kOk;
 }
 
+namespace {
+int encode_2d_f32(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                  uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle);
+}  // namespace
+
 int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
                              uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
                              uint32_t box_outer) {
+  return encode_2d_f32(map, base, inner, outer, row_pitch_bytes, box_inner, box_outer,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int encode_tmap_2d_f32_sw128_atom32(CUtensorMap *map, const void *base, uint64_t inner,
+                                    uint64_t outer, uint64_t row_pitch_bytes,
+                                    uint32_t box_inner, uint32_t box_outer) {
+  return encode_2d_f32(map, base, inner, outer, row_pitch_bytes, box_inner, box_outer,
+                       CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
+namespace {
+int encode_2d_f32(CUtensorMap *map, const void *base, uint64_t inner, uint64_t outer,
+                  uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return kErrInternal;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_pitch_bytes & 15u) != 0)
@@ -121,11 +142,11 @@ int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims,
-                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? kOk : kErrInternal;
 }
+}  // namespace
 
 int encode_tmap_im2col_nhwc_f32_sw128(CUtensorMap *map, const void *base, uint64_t c,
                                      uint64_t w, uint64_t h, uint64_t n, int lower_w,

@@ -44,6 +44,10 @@ int ensure_dynamic_smem(const void *func, int bytes);
 int encode_tmap_2d_f32_sw128(CUtensorMap *map, const void *base, uint64_t inner,
                              uint64_t outer, uint64_t row_pitch_bytes, uint32_t box_inner,
                              uint32_t box_outer);
+// The same with the 128-byte swizzle of 32-byte atoms (MN-major tf32 operands).
+int encode_tmap_2d_f32_sw128_atom32(CUtensorMap *map, const void *base, uint64_t inner,
+                                    uint64_t outer, uint64_t row_pitch_bytes,
+                                    uint32_t box_inner, uint32_t box_outer);
 
 // 4-D NHWC fp32 im2col tensor map (dims {c, w, h, n}, densely packed): each
 // load gathers `pixels` output pixels x `channels` channels, walking the

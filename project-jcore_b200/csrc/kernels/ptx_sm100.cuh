@@ -20,7 +20,7 @@ enum : int {
   kStatusTimeoutMma = 102,       // MMA warp waited too long for a filled stage
   kStatusTimeoutEpilogue = 103,  // epilogue waited too long for an accumulator
   kStatusTimeoutAccFree = 104,   // MMA warp waited too long for a drained accumulator
-  kStatusTimeoutStage = 105,     // window kernel warp waited too long for a staged batch
+  kStatusTimeoutStage = 105,     // a consumer warp waited too long for a staged batch
 };
 
 // 4 s of device time: orders of magnitude above any legitimate stage wait.
@@ -334,6 +334,26 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_byte_addr) {
 // Instruction descriptor for kind::tf32 with fp32 accumulation, both operands
 // K-major: D format F32 at [4,6), A/B format TF32 (=2) at [7,10)/[10,13),
 // N>>3 at [17,23), M>>4 at [24,29).
+// MN-major fp32 (tf32) operand. The only MN-major shared-memory layout the
+// tensor core takes for 32-bit types is the 128-byte swizzle with 32-byte
+// atoms (descriptor layout type 1; TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B):
+// 32 values along M/N per 128-byte row, rows along K, the swizzle repeating
+// every 4 rows. `lbo_bytes` between 32-wide M/N atoms, 512 bytes between
+// 4-row K groups; a K = 8 step adds 1024 bytes (+64 in the address field).
+// (Measured on this part: the plain 128-byte swizzle reads as zeros.)
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128_32b(uint32_t smem_byte_addr,
+                                                           uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_byte_addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(512u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(1u) << 61;
+  return d;
+}
+// Instruction descriptor bit of an MN-major B operand.
+constexpr uint32_t kUmmaIdescBMajorMN = 1u << 16;
+
 __host__ __device__ constexpr uint32_t umma_idesc_tf32(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);

@@ -140,15 +140,20 @@ extern "C" int npl_matmul(const npl_tensor_t *A, const npl_tensor_t *B, npl_tens
   const float *a = call.input(A->data, batch * M * K * 4);
   const float *b = call.input(B->data, b_elems * 4);
   float *c = call.output(C->data, batch * M * N * 4, beta != 0.0f);
-  const size_t ws = nplk_gemm_workspace_size(M, N, K);
-  void *w = call.scratch(ws);
+  // The hi/lo operand workspace (805 MB for 8192x4096x16384); when the device
+  // cannot spare it, nplk_gemm reads A and B in place (raw operand form).
+  size_t ws = nplk_gemm_workspace_size(M, N, K);
+  void *w = call.try_scratch(ws);
+  if (!w) ws = 0;
   if (call.status()) return call.finish(nullptr, 0, 0, nullptr);
   const unsigned flags = npl::tf32_fast_mode() ? NPLK_GEMM_TF32_FAST : 0u;
   call.start_timer();
   for (size_t i = 0; i < batch && !call.status(); ++i) {
-    call.fail(nplk_gemm(call.stream(), M, N, K, alpha, a + i * M * K, K,
-                        b + (b_batched ? i * K * N : 0), N, beta, c + i * M * N, N, nullptr,
-                        NPLK_ACT_NONE, 0.0f, flags, w, ws, nullptr));
+    const int rc = nplk_gemm(call.stream(), M, N, K, alpha, a + i * M * K, K,
+                             b + (b_batched ? i * K * N : 0), N, beta, c + i * M * N, N,
+                             nullptr, NPLK_ACT_NONE, 0.0f, flags, w, ws, nullptr);
+    // No workspace and operands the raw form cannot read in place: out of memory.
+    call.fail(!w && rc == NPL_ERR_INVALID_ARG ? NPL_ERR_OOM : rc);
   }
   call.stop_timer();
   return call.finish(stats, 2.0 * batch * M * N * K,

@@ -254,6 +254,17 @@ void *Call::scratch(size_t bytes) {
   return d;
 }
 
+void *Call::try_scratch(size_t bytes) {
+  if (status_) return nullptr;
+  void *d = nullptr;
+  if (cudaMallocAsync(&d, bytes < 256 ? 256 : bytes, stream_) != cudaSuccess) {
+    cudaGetLastError();  // an allocation failure is not sticky; clear it
+    return nullptr;
+  }
+  scratch_.push_back(d);
+  return d;
+}
+
 void Call::start_timer() {
   if (!status_ && cudaEventRecord(ev0_, stream_) == cudaSuccess) timed_ = true;
 }

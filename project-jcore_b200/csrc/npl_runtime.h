@@ -65,6 +65,9 @@ class Call {
   float *param_out(float *p, size_t count);
   // Device scratch for this call.
   void *scratch(size_t bytes);
+  // Like scratch(), but an allocation failure returns nullptr without failing
+  // the call (for callers with a path that needs no scratch).
+  void *try_scratch(size_t bytes);
 
   void start_timer();
   void stop_timer();

@@ -36,6 +36,8 @@ NPL_MAX_DIMS = 8
 NPLK_CONV_ALGO_AUTO, NPLK_CONV_ALGO_DIRECT, NPLK_CONV_ALGO_IM2COL = 0, 1, 2
 NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER = 3, 4
 NPLK_GEMM_TF32_FAST = 1
+NPLK_GEMM_SPLIT_OPERANDS = 2
+NPLK_GEMM_RAW_OPERANDS = 4
 
 
 class NplConfig(C.Structure):

@@ -152,3 +152,66 @@ def test_gemm_config5_device_sampled_rows():
     ref = a64 @ B.double().cpu().numpy() + bias.double().cpu().numpy()[None, :]
     got = Cm[rows].cpu().numpy()
     assert S.normwise_err(got, ref) < TOL
+
+
+FORM_SHAPES = [(128, 128, 32), (256, 192, 96), (300, 260, 100), (64, 40, 8), (129, 100, 36),
+               (1024, 1024, 1024), (640, 4096, 256)]
+
+
+@pytest.mark.parametrize("form", ["raw", "split"])
+@pytest.mark.parametrize("m,n,k", FORM_SHAPES)
+def test_gemm_operand_forms(m, n, k, form):
+    # Both operand forms (raw: A and B read in place, lo parts formed in shared
+    # memory; split: hi/lo copies in the workspace) with alpha, beta, bias and
+    # ReLU in the epilogue and padded leading dimensions, against fp64.
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator(device="cuda").manual_seed(m + n + k)
+    lda, ldb, ldc = k + 4, n + 8, n + 4
+    A = (torch.rand(m, lda, device="cuda", generator=gen) * 2 - 1)
+    B = (torch.rand(k, ldb, device="cuda", generator=gen) * 2 - 1)
+    C0 = torch.rand(m, ldc, device="cuda", generator=gen) - 0.5
+    bias = torch.rand(n, device="cuda", generator=gen) - 0.5
+    Cm = C0.clone()
+    flags = nb.NPLK_GEMM_RAW_OPERANDS if form == "raw" else nb.NPLK_GEMM_SPLIT_OPERANDS
+    ws = lib.nplk_gemm_workspace_size(m, n, k) if form == "split" else 0
+    work = torch.empty(ws // 4 + 64, device="cuda") if ws else None
+    rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 0.75, S.dptr(A), lda, S.dptr(B), ldb, 0.5,
+                       S.dptr(Cm), ldc, S.dptr(bias), nb.NPL_ACT_RELU, 0.0, flags,
+                       S.dptr(work) if work is not None else None, ws, None)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(S.cuda_stream()) == 0
+    a64 = A[:, :k].double().cpu().numpy()
+    b64 = B[:, :n].double().cpu().numpy()
+    ref = 0.75 * (a64 @ b64) + 0.5 * C0[:, :n].double().cpu().numpy() + \
+        bias.double().cpu().numpy()[None, :]
+    ref = np.maximum(ref, 0.0)
+    got = Cm.cpu().numpy()
+    assert S.normwise_err(got[:, :n], ref) < TOL
+    assert np.array_equal(got[:, n:], C0[:, n:].cpu().numpy())  # padding untouched
+
+
+def test_gemm_raw_form_infinity_and_eligibility():
+    # An infinite entry of A gives an infinite row (its lo part is 0, not
+    # inf - inf); forcing the raw form on operands TMA cannot read in place
+    # (lda not a multiple of 4) is refused.
+    import torch
+    lib = S.gpu_lib()
+    m, n, k = 256, 128, 64
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.rand(m, k, device="cuda", generator=gen) + 0.5
+    B = torch.rand(k, n, device="cuda", generator=gen) + 0.5
+    A[3, 7] = float("inf")
+    Cm = torch.zeros(m, n, device="cuda")
+    rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 1.0, S.dptr(A), k, S.dptr(B), n, 0.0,
+                       S.dptr(Cm), n, None, 0, 0.0, nb.NPLK_GEMM_RAW_OPERANDS, None, 0, None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    got = Cm.cpu().numpy()
+    assert np.all(np.isposinf(got[3]))
+    assert np.all(np.isfinite(np.delete(got, 3, axis=0)))
+    A2 = torch.rand(m, k + 1, device="cuda", generator=gen)
+    rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 1.0, S.dptr(A2), k + 1, S.dptr(B), n, 0.0,
+                       S.dptr(Cm), n, None, 0, 0.0, nb.NPLK_GEMM_RAW_OPERANDS, None, 0, None)
+    assert rc == nb.NPL_ERR_UNSUPPORTED
