@@ -370,8 +370,18 @@ __device__ __forceinline__ float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+// x = hi + lo with hi = rna_tf32(x). +-inf splits into (x, 0) -- not
+// (inf, inf - inf = NaN) -- and a finite x that rounds up to inf is truncated
+// instead, so that hi + lo keeps x's value class.
 __device__ __forceinline__ void tf32_split(float x, float &hi, float &lo) {
   hi = tf32_rna(x);
+  if (fabsf(hi) == __int_as_float(0x7f800000)) {
+    if (fabsf(x) != __int_as_float(0x7f800000)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    else {
+      lo = 0.0f;
+      return;
+    }
+  }
   lo = tf32_rna(x - hi);
 }
 

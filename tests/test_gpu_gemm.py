@@ -192,10 +192,13 @@ def test_gemm_operand_forms(m, n, k, form):
     assert np.array_equal(got[:, n:], C0[:, n:].cpu().numpy())  # padding untouched
 
 
-def test_gemm_raw_form_infinity_and_eligibility():
-    # An infinite entry of A gives an infinite row (its lo part is 0, not
-    # inf - inf); forcing the raw form on operands TMA cannot read in place
-    # (lda not a multiple of 4) is refused.
+@pytest.mark.parametrize("form", ["raw", "split"])
+def test_gemm_infinity_and_raw_eligibility(form):
+    # An infinite entry of A stays confined to its row in both operand forms
+    # (its own lo part is 0, not inf - inf; the row itself holds +inf or NaN:
+    # 3xTF32 forms inf * lo(B), which is NaN where lo(B) is 0). Forcing the raw
+    # form on operands TMA cannot read in place (lda not a multiple of 4) is
+    # refused.
     import torch
     lib = S.gpu_lib()
     m, n, k = 256, 128, 64
@@ -204,13 +207,19 @@ def test_gemm_raw_form_infinity_and_eligibility():
     B = torch.rand(k, n, device="cuda", generator=gen) + 0.5
     A[3, 7] = float("inf")
     Cm = torch.zeros(m, n, device="cuda")
+    ws = lib.nplk_gemm_workspace_size(m, n, k) if form == "split" else 0
+    work = torch.empty(ws // 4 + 64, device="cuda") if ws else None
+    flags = nb.NPLK_GEMM_RAW_OPERANDS if form == "raw" else nb.NPLK_GEMM_SPLIT_OPERANDS
     rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 1.0, S.dptr(A), k, S.dptr(B), n, 0.0,
-                       S.dptr(Cm), n, None, 0, 0.0, nb.NPLK_GEMM_RAW_OPERANDS, None, 0, None)
+                       S.dptr(Cm), n, None, 0, 0.0, flags,
+                       S.dptr(work) if work is not None else None, ws, None)
     assert rc == 0
     torch.cuda.synchronize()
     got = Cm.cpu().numpy()
-    assert np.all(np.isposinf(got[3]))
+    assert not np.isfinite(got[3]).any() and not np.isneginf(got[3]).any()
     assert np.all(np.isfinite(np.delete(got, 3, axis=0)))
+    if form == "split":
+        return
     A2 = torch.rand(m, k + 1, device="cuda", generator=gen)
     rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 1.0, S.dptr(A2), k + 1, S.dptr(B), n, 0.0,
                        S.dptr(Cm), n, None, 0, 0.0, nb.NPLK_GEMM_RAW_OPERANDS, None, 0, None)
