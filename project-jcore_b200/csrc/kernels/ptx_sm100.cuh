@@ -108,6 +108,18 @@ __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
   return true;
 }
 
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// global to shared memory on the async proxy; completion is counted on `bar`
+// (transaction bytes). No multicast.
+__device__ __forceinline__ void bulk_load_g2s(void *dst, const void *src, uint32_t bytes,
+                                              uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor-core operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {

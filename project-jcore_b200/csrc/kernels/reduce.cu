@@ -6,6 +6,7 @@
 #include <math_constants.h>
 
 #include "nplk_host.h"
+#include "ptx_sm100.cuh"
 
 namespace nplk {
 
@@ -147,6 +148,135 @@ __global__ void layernorm_rows_kernel(const float *__restrict__ x, float *__rest
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int j = threadIdx.x + blockDim.x * i;
+      if (j < c4) {
+        float4 o;
+        const float g0 = gamma ? gamma[4 * j] : 1.0f, g1 = gamma ? gamma[4 * j + 1] : 1.0f,
+                    g2 = gamma ? gamma[4 * j + 2] : 1.0f, g3 = gamma ? gamma[4 * j + 3] : 1.0f;
+        const float b0 = beta ? beta[4 * j] : 0.0f, b1 = beta ? beta[4 * j + 1] : 0.0f,
+                    b2 = beta ? beta[4 * j + 2] : 0.0f, b3 = beta ? beta[4 * j + 3] : 0.0f;
+        o.x = g0 * ((v[i].x - mean) * inv) + b0;
+        o.y = g1 * ((v[i].y - mean) * inv) + b1;
+        o.z = g2 * ((v[i].z - mean) * inv) + b2;
+        o.w = g3 * ((v[i].w - mean) * inv) + b3;
+        yr[j] = o;
+      }
+    }
+  }
+}
+
+// Long rows (2 K..16 K elements, a multiple of 4, 16-byte aligned): the
+// arithmetic of layernorm_rows_kernel fed by a warp-specialised ring. One
+// producer lane stages whole rows (one bulk copy each) into `stages`
+// shared-memory stages; the 16 consumer warps form G groups (kG = 1, 2 or 4)
+// that each take every G-th row: a group reads its row into registers,
+// releases the stage at once (its own named barrier), reduces and writes,
+// while the other groups and the next rows' copies proceed. With G = 1 (16 K
+// rows) the thread-to-element mapping is layernorm_rows_kernel's with 512
+// threads, so the results agree bit for bit.
+constexpr int kLnWarps = 16;
+constexpr int kLnThreads = (kLnWarps + 1) * 32;
+
+template <int kG>
+__device__ __forceinline__ void ln_group_sync(int group) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "n"(kLnWarps * 32 / kG) : "memory");
+}
+
+// Sum over the group's warps; every thread of the group gets the result.
+template <int kG>
+__device__ __forceinline__ float ln_group_sum(float v, float *red, int group) {
+  constexpr int kGW = kLnWarps / kG;  // warps per group
+  const int lane = threadIdx.x & 31, gw = (threadIdx.x >> 5) % kGW;
+  v = warp_sum(v);
+  if (lane == 0) red[group * kGW + gw] = v;
+  ln_group_sync<kG>(group);
+  float t = lane < kGW ? red[group * kGW + lane] : 0.0f;
+  t = warp_sum(t);
+  ln_group_sync<kG>(group);  // red is written again by the next reduction
+  return t;
+}
+
+template <int NV, int kG>
+__global__ void __launch_bounds__(kLnThreads, 1)
+    layernorm_ring_kernel(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
+                          int cols, const float *__restrict__ gamma,
+                          const float *__restrict__ beta, float eps, int stages, int *status) {
+  extern __shared__ __align__(128) uint8_t smem_ln[];
+  float *st = reinterpret_cast<float *>(smem_ln);
+  uint64_t *full = reinterpret_cast<uint64_t *>(st + static_cast<int64_t>(stages) * cols);
+  uint64_t *empty = full + stages;
+  float *red = reinterpret_cast<float *>(empty + stages);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(red + 32);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int64_t nk = rows > blockIdx.x ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+  if (warp == kLnWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int64_t k = 0;
+      for (; k < nk; ++k) {
+        const int s = static_cast<int>(k % stages);
+        const uint32_t ph = static_cast<uint32_t>(k / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status, kStatusTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&full[s], row_bytes);
+        bulk_load_g2s(st + static_cast<int64_t>(s) * cols,
+                      x + (blockIdx.x + k * gridDim.x) * static_cast<int64_t>(cols), row_bytes,
+                      &full[s]);
+      }
+      for (int64_t j = k > stages ? k - stages : 0; j < k; ++j)
+        mbar_drain(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u);
+    }
+    return;
+  }
+  // ---------------- consumers ----------------
+  constexpr int kGT = kLnWarps * 32 / kG;  // threads per group
+  const int group = threadIdx.x / kGT;
+  const int t = threadIdx.x - group * kGT;
+  const int c4 = cols >> 2;
+  for (int64_t k = group; k < nk; k += kG) {
+    const int s = static_cast<int>(k % stages);
+    const uint32_t ph = static_cast<uint32_t>(k / stages) & 1u;
+    if (!mbar_wait(&full[s], ph, abort_flag, status, kStatusTimeoutStage)) break;
+    const float4 *xr = reinterpret_cast<const float4 *>(st + static_cast<int64_t>(s) * cols);
+    float4 v[NV];
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = t + kGT * i;
+      if (j < c4) {
+        v[i] = xr[j];
+        sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      }
+    }
+    ln_group_sync<kG>(group);  // every thread of the group holds its part of the row
+    if (t == 0) mbar_arrive(&empty[s]);
+    const float mean = ln_group_sum<kG>(sum, red, group) / static_cast<float>(cols);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = t + kGT * i;
+      if (j < c4) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean,
+                    d = v[i].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+      }
+    }
+    const float var = ln_group_sum<kG>(q, red, group) / static_cast<float>(cols);
+    const float inv = 1.0f / sqrtf(var + eps);
+    float4 *yr = reinterpret_cast<float4 *>(
+        y + (blockIdx.x + k * gridDim.x) * static_cast<int64_t>(cols));
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = t + kGT * i;
       if (j < c4) {
         float4 o;
         const float g0 = gamma ? gamma[4 * j] : 1.0f, g1 = gamma ? gamma[4 * j + 1] : 1.0f,
@@ -346,7 +476,43 @@ extern "C" int nplk_layer_norm(void *stream, int64_t rows, int64_t cols, const f
   if (rows <= 0 || cols <= 0 || !x || !y) return kErrInvalidArg;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t rows_grid = rows < 65535 * 16 ? rows : 65535 * 16;
-  if (cols % 4 == 0 && aligned16(x) && aligned16(y) && cols <= 512 * 4 * 16) {
+  if (cols % 4 == 0 && aligned16(x) && aligned16(y) && cols >= 2048 && cols <= 16384) {
+    // Rows of 8..64 KB through the ring: up to 8 stages in ~200 KB (3 for
+    // 64 KB rows); the grid is as many CTAs as are resident.
+    const int64_t row_bytes = cols * 4;
+    int stages = static_cast<int>(200 * 1024 / row_bytes);
+    if (stages > 8) stages = 8;
+    const size_t smem = static_cast<size_t>(stages) * row_bytes + 2 * 8 * 8 + 32 * 4 + 16;
+    // Groups: 16 K rows take all 16 warps; 8 K rows two groups of 8; shorter
+    // rows four groups of 4 (each thread then holds up to 8 float4).
+    const int G = cols > 8192 ? 1 : cols > 4096 ? 2 : 4;
+    const int nv = static_cast<int>(ceil_div(cols / 4, int64_t(kLnWarps * 32 / G)));
+    int *status = device_status_word();
+    const int ci = static_cast<int>(cols);
+    auto go = [&](auto kernel) -> int {
+      if (int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel),
+                                       static_cast<int>(smem)))
+        return rc;
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLnThreads, smem) !=
+              cudaSuccess ||
+          per_sm < 1)
+        per_sm = 1;
+      int64_t blocks = static_cast<int64_t>(sm_count()) * per_sm;
+      if (blocks > rows) blocks = rows;
+      kernel<<<static_cast<unsigned>(blocks), kLnThreads, smem, s>>>(x, y, rows, ci, gamma, beta,
+                                                                     eps, stages, status);
+      return 0;
+    };
+    int rc;
+    if (G == 1)
+      rc = go(layernorm_ring_kernel<8, 1>);
+    else if (G == 2)
+      rc = go(layernorm_ring_kernel<8, 2>);
+    else
+      rc = nv <= 4 ? go(layernorm_ring_kernel<4, 4>) : go(layernorm_ring_kernel<8, 4>);
+    if (rc) return rc;
+  } else if (cols % 4 == 0 && aligned16(x) && aligned16(y) && cols <= 512 * 4 * 16) {
     const int64_t c4 = cols / 4;
     int threads = 512;
     while (threads > 32 && threads / 2 >= c4) threads /= 2;

@@ -169,17 +169,6 @@ __device__ __forceinline__ float window_out(const float *xp, const float *wp, in
   }
 }
 
-// Bulk copy of `bytes` (a multiple of 16) from global to shared memory on the
-// async proxy; completion is counted on `bar` (transaction bytes).
-__device__ __forceinline__ void bulk_load_g2s(void *dst, const void *src, uint32_t bytes,
-                                              uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 constexpr int kBandWarps = 4;                      // consumer warps per CTA
 constexpr int kBandThreads = (kBandWarps + 1) * 32;  // + one producer warp
 constexpr int kBandStages = 8;                     // staged batches per CTA

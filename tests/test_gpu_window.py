@@ -162,3 +162,47 @@ def test_pool_bands_inside_padding():
         got = y.cpu().numpy()
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)) or \
             S.normwise_err(got, ref) < 1e-6
+
+
+@pytest.mark.parametrize("offset", [0, 3])
+@pytest.mark.parametrize("planes,hw", [(131072 // 64, 196), (1000, 49), (777, 63), (50, 1776),
+                                       (40, 3136), (5, 1)])
+def test_global_avg_pool_plane_sizes(planes, hw, offset):
+    # Plane sizes a multiple of 4 (16-byte loads, several planes per warp)
+    # and not, an unaligned start when offset != 0, and large planes.
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator(device="cuda").manual_seed(planes + hw + offset)
+    x = _offset_tensor(torch, (planes, hw), gen, offset)
+    y = torch.full((planes,), float("nan"), device="cuda")
+    assert lib.nplk_global_avg_pool(S.cuda_stream(), planes, hw, S.dptr(x), S.dptr(y)) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(S.cuda_stream()) == 0
+    got = y.cpu().numpy()
+    ref = S.o_gap(x.cpu().numpy().reshape(planes, 1, hw))[:, 0]
+    assert not np.isnan(got).any()
+    assert S.normwise_err(got, ref) < 1e-6
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("rows,cols", [(1, 2048), (7, 4100), (300, 8192), (33, 12000),
+                                       (150, 16384), (5, 16388)])
+def test_layer_norm_long_rows(rows, cols, offset):
+    # Rows of 2 K..16 K elements (a multiple of 4, aligned) go through the
+    # staged ring kernel; an unaligned start or longer rows take the
+    # register-row or three-pass kernels.
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator(device="cuda").manual_seed(rows + cols + offset)
+    x = _offset_tensor(torch, (rows, cols), gen, offset) * 3 + 1
+    y = torch.full((rows, cols), float("nan"), device="cuda")
+    gamma = torch.rand(cols, device="cuda", generator=gen) + 0.5
+    beta = torch.rand(cols, device="cuda", generator=gen) - 0.5
+    assert lib.nplk_layer_norm(S.cuda_stream(), rows, cols, S.dptr(x), S.dptr(y), S.dptr(gamma),
+                               S.dptr(beta), 1e-5) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(S.cuda_stream()) == 0
+    got = y.cpu().numpy()
+    ref = S.o_layer_norm(x.cpu().numpy(), cols, gamma.cpu().numpy(), beta.cpu().numpy())
+    assert not np.isnan(got).any()
+    assert S.normwise_err(got, ref) < 1e-5
