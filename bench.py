@@ -441,6 +441,25 @@ def bandwidth_also(lib, local_rank, reps=10):
         ("layer_norm 8192x4096", rows.numel() * 8,
          lambda: lib.nplk_layer_norm(s, 8192, 4096, p(rows), p(rows_y), None, None, 1e-5)),
     ]
+    # The depthwise -> BN -> ReLU -> GAP -> softmax chain on [256,512,14,14]
+    # (BN in place on the depthwise output, ReLU in place, softmax over the
+    # 512 channels of each image), back to back on one stream after one L2
+    # flush; bytes: each kernel's input read once and output written once.
+    y2 = torch.empty_like(x)
+    sm_out = torch.empty(n * c, device=dev)
+    chain_bytes = (nx * 8 + w.numel() * 4) + nx * 8 + nx * 8 + (nx * 4 + n * c * 4) + n * c * 8
+
+    def chain():
+        rcs = (lib.nplk_depthwise_conv2d(s, C.byref(g), p(x), p(w), None, p(y)),
+               lib.nplk_batch_norm_infer(s, n, c, hw * hw, p(y), p(y2), p(bn[0]), p(bn[1]),
+                                         p(bn[2]), p(bn[3]), 1e-5),
+               lib.nplk_activation(s, nx, p(y2), p(y2), 1, 0.0, 0),
+               lib.nplk_global_avg_pool(s, n * c, hw * hw, p(y2), p(gap)),
+               lib.nplk_softmax(s, n, c, 1, p(gap), p(sm_out)))
+        return max(abs(r) for r in rcs)
+
+    cases.append(("chain depthwise->BN->ReLU->GAP->softmax [256,512,14,14]", chain_bytes,
+                  chain))
     hbm, _, src = measured_peaks()
     out = {}
     # Size-matched reference: a device copy of the same 103 MB tensor (103 MB
