@@ -10,6 +10,8 @@ and checks the kernel status word.
     python -m npl_b200.profile_cases gemm      # 4096x4096x8192 3xTF32 GEMM
     python -m npl_b200.profile_cases chain     # depthwise, BN, ReLU, GAP, softmax 256x512x14x14
     python -m npl_b200.profile_cases layernorm # 8192 x 16384 rows
+    python -m npl_b200.profile_cases pool      # max pool 3x3/s2 [32,64,112,112] -> 56x56
+    python -m npl_b200.profile_cases gemm_raw  # the 4096x4096x8192 GEMM, raw operand form
 
 Run from the package directory (``project-jcore_b200``) or with it on sys.path.
 """
@@ -59,17 +61,17 @@ def case_stem(reps: int = 3):
     case_conv(reps, n=16, c=3, hw=224, cout=64, k=7, stride=2, pad=3)
 
 
-def case_gemm(reps: int = 3, m: int = 4096, n: int = 4096, k: int = 8192):
+def case_gemm(reps: int = 3, m: int = 4096, n: int = 4096, k: int = 8192, raw: bool = False):
     torch, lib, s = _setup()
     gen = torch.Generator(device="cuda").manual_seed(0)
     a = torch.randn(m, k, device="cuda", generator=gen)
     b = torch.randn(k, n, device="cuda", generator=gen) / 64.0
     c = torch.empty(m, n, device="cuda")
-    ws = lib.nplk_gemm_workspace_size(m, n, k)
-    work = torch.empty(ws // 4 + 64, device="cuda")
+    ws = 0 if raw else lib.nplk_gemm_workspace_size(m, n, k)
+    work = None if raw else torch.empty(ws // 4 + 64, device="cuda")
     for _ in range(reps):
         rc = lib.nplk_gemm(s, m, n, k, 1.0, _p(a), k, _p(b), n, 0.0, _p(c), n, None, 0, 0.0, 0,
-                           _p(work), ws, None)
+                           _p(work) if work is not None else None, ws, None)
         assert rc == 0, rc
     torch.cuda.synchronize()
     assert lib.nplk_read_status(s) == 0
@@ -97,6 +99,17 @@ def case_chain(reps: int = 3):
     torch.cuda.synchronize()
 
 
+def case_pool(reps: int = 3):
+    torch, lib, s = _setup()
+    x = torch.randn(32, 64, 112, 112, device="cuda")
+    y = torch.empty(32, 64, 56, 56, device="cuda")
+    for _ in range(reps):
+        assert lib.nplk_pool2d(s, 32, 64, 112, 112, 3, 3, 2, 2, 1, 1, 56, 56, 0, 0, _p(x),
+                               _p(y)) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+
+
 def case_layernorm(reps: int = 3):
     torch, lib, s = _setup()
     x = torch.randn(8192, 16384, device="cuda")
@@ -111,7 +124,8 @@ CASES = {"conv": case_conv,
          "conv_window_tma": lambda: case_conv(algo=3),
          "conv_s2": lambda: case_conv(cout=128, stride=2),
          "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
-         "layernorm": case_layernorm}
+         "layernorm": case_layernorm, "pool": case_pool,
+         "gemm_raw": lambda: case_gemm(raw=True)}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else "conv"
