@@ -23,7 +23,12 @@ Reported (one JSON line on rank 0):
             rate and 3xTF32 issues three TF32 products per output product);
   cpu_baseline  the reference's own CPU code (oracle/_ref, built from the
             reference sources) on the same workload, all host threads;
-  also      the large fp32 GEMM [8192x4096]@[4096x16384] (+bias via beta=1).
+  also      the other workloads on the GPU -- the large fp32 GEMM
+            [8192x4096]@[4096x16384] (+bias via beta=1, then ReLU and layer
+            norm), the 1024^3 GEMM, the 7x7/s2 stem conv + max pool, the
+            bandwidth kernels and their depthwise->BN->ReLU->GAP->softmax
+            chain -- and (cpu_reference_rows) the reference's CPU code on
+            bounded samples of the same workloads, scaled to full size.
 
 --impl reference runs only the reference CPU arm on the same workload.
 """
@@ -148,11 +153,13 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # reference CPU arm
 # ---------------------------------------------------------------------------
-def reference_cpu(steps: int, warmup: int):
+def reference_cpu(steps: int, warmup: int, rows: bool = False):
     """Times the reference's own CPU implementation of the step (its
     npl_conv2d_bn_activation -- which runs the conv only -- followed by its
     npl_batch_norm and npl_relu) with all host threads. Returns
-    (TFLOP/s, cores, sample, median seconds)."""
+    (TFLOP/s, cores, sample, median seconds, rows) where rows (with
+    rows=True) holds the reference's times on bounded samples of the other
+    workloads (_reference_cpu_rows)."""
     ref_lib = REPO / "oracle" / "_ref" / "libnpl_ref.so"
     if not ref_lib.exists():
         return None
@@ -161,7 +168,7 @@ def reference_cpu(steps: int, warmup: int):
     saved = os.dup(1)
     os.dup2(devnull, 1)  # the reference prints on init and on every activation call
     try:
-        return _reference_cpu_timed(ref_lib, steps, warmup)
+        return _reference_cpu_timed(ref_lib, steps, warmup, rows)
     finally:
         sys.stdout.flush()
         os.dup2(saved, 1)
@@ -169,7 +176,121 @@ def reference_cpu(steps: int, warmup: int):
         os.close(saved)
 
 
-def _reference_cpu_timed(ref_lib, steps, warmup):
+def _reference_cpu_rows(lib, cores):
+    """The reference's CPU code on the other workloads, each on a bounded
+    sample (median of 3 calls after one warm-up), scaled to the full workload
+    by the sample's share of it: the 1024^3 GEMM in full; the stem on 2 of 128
+    images (its conv -- conv only -- then its batch norm, ReLU and 3x3/s2 max
+    pool); the depthwise -> BN -> ReLU -> GAP -> softmax chain on 16 of 256
+    images; the 8192x4096x16384 GEMM (+ bias via beta=1) with ReLU and layer
+    norm on 512 of 8192 rows."""
+    rng = np.random.default_rng(0)
+    keep = []
+
+    def T(a):
+        keep.append(a)
+        return nb.tensor(lib, a.ctypes.data, a.shape)
+
+    def timed(fn, reps=3):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    def ok(rc):
+        assert rc == 0, rc
+
+    out = {}
+    f32 = np.float32
+    # d1: 1024^3
+    a = rng.uniform(-1, 1, (1024, 1024)).astype(f32)
+    b = rng.uniform(-1, 1, (1024, 1024)).astype(f32)
+    ta, tb, tc = T(a), T(b), T(np.zeros((1024, 1024), f32))
+    sec = timed(lambda: ok(lib.npl_matmul(C.byref(ta), C.byref(tb), C.byref(tc), C.c_float(1.0),
+                                          C.c_float(0.0), None)))
+    out["gemm_1024"] = {"us": round(sec * 1e6, 1), "TFLOP/s": round(2 * 1024 ** 3 / sec / 1e12, 5),
+                        "sample": "full workload"}
+    # d3: stem on 2 of 128 images
+    ns = 2
+    x = rng.uniform(-1, 1, (ns, 3, 224, 224)).astype(f32)
+    w = rng.normal(0, np.sqrt(2 / 147), (64, 3, 7, 7)).astype(f32)
+    g, be = rng.uniform(0.5, 1.5, 64).astype(f32), rng.uniform(-0.1, 0.1, 64).astype(f32)
+    mu, va = rng.normal(0, 0.1, 64).astype(f32), rng.uniform(0.5, 1.5, 64).astype(f32)
+    keep.extend([g, be, mu, va])
+    tx, tw = T(x), T(w)
+    tconv, tbn = T(np.zeros((ns, 64, 112, 112), f32)), T(np.zeros((ns, 64, 112, 112), f32))
+    tpool = T(np.zeros((ns, 64, 56, 56), f32))
+    cp = nb.conv_params(7, 7, 2, 3, padding=nb.NPL_PAD_EXPLICIT)
+    bnp = nb.NplBatchnormParams(mu.ctypes.data, va.ctypes.data, g.ctypes.data, be.ctypes.data,
+                                1e-5, 0, 0.1)
+    pp = nb.NplPoolingParams(3, 3, 2, 2, 1, 1, nb.NPL_POOL_MAX, 0)
+
+    def stem():
+        ok(lib.npl_conv2d_bn_activation(C.byref(tx), C.byref(tw), None, C.byref(cp), C.byref(bnp),
+                                        nb.NPL_ACT_RELU, C.byref(tconv), None))
+        ok(lib.npl_batch_norm(C.byref(tconv), C.byref(bnp), C.byref(tbn), None))
+        ok(lib.npl_relu(C.byref(tbn), C.byref(tbn), None))
+        ok(lib.npl_pooling(C.byref(tbn), C.byref(pp), C.byref(tpool), None))
+
+    sec = timed(stem) * (128 / ns)
+    out["stem"] = {"ms_full_workload": round(sec * 1e3, 2),
+                   "conv_TFLOP/s": round(2.0 * 128 * 64 * 3 * 112 * 112 * 49 / sec / 1e12, 5),
+                   "sample": f"{ns} of 128 images, scaled"}
+    # d4: chain on 16 of 256 images
+    ns = 16
+    x = rng.normal(0, 1, (ns, 512, 14, 14)).astype(f32)
+    w = rng.normal(0, 0.3, (512, 1, 3, 3)).astype(f32)
+    g, be = rng.uniform(0.5, 1.5, 512).astype(f32), rng.uniform(-0.1, 0.1, 512).astype(f32)
+    mu, va = rng.normal(0, 0.1, 512).astype(f32), rng.uniform(0.5, 1.5, 512).astype(f32)
+    keep.extend([g, be, mu, va])
+    tx, tw = T(x), T(w)
+    tdw, tb2 = T(np.zeros_like(x)), T(np.zeros_like(x))
+    tgap, tsm = T(np.zeros((ns, 512), f32)), T(np.zeros((ns, 512), f32))
+    dp = nb.conv_params(3, 3, 1, 1, padding=nb.NPL_PAD_EXPLICIT)
+    bnp2 = nb.NplBatchnormParams(mu.ctypes.data, va.ctypes.data, g.ctypes.data, be.ctypes.data,
+                                 1e-5, 0, 0.1)
+
+    def chain():
+        ok(lib.npl_depthwise_conv2d(C.byref(tx), C.byref(tw), None, C.byref(dp), C.byref(tdw),
+                                    None))
+        ok(lib.npl_batch_norm(C.byref(tdw), C.byref(bnp2), C.byref(tb2), None))
+        ok(lib.npl_relu(C.byref(tb2), C.byref(tb2), None))
+        ok(lib.npl_global_avg_pool(C.byref(tb2), C.byref(tgap), None))
+        ok(lib.npl_softmax(C.byref(tgap), 1, C.byref(tsm), None))
+
+    sec = timed(chain) * (256 / ns)
+    out["bandwidth_chain"] = {"us_full_workload": round(sec * 1e6, 1),
+                              "GB/s": round(720914432 / sec / 1e9, 2),
+                              "sample": f"{ns} of 256 images, scaled"}
+    # d5: GEMM + bias (beta=1) + ReLU + layer norm on 512 of 8192 rows
+    ms_, k_, n_ = 512, 4096, 16384
+    a = rng.normal(0, 1, (ms_, k_)).astype(f32)
+    b = (rng.normal(0, 1, (k_, n_)) / 64.0).astype(f32)
+    bias = rng.normal(0, 0.02, n_).astype(f32)
+    c = np.empty((ms_, n_), f32)
+    ta, tb, tcm, ty = T(a), T(b), T(c), T(np.zeros((ms_, n_), f32))
+    lnp = nb.NplLayernormParams(None, None, 1e-5, n_)
+
+    def big():
+        c[:] = bias[None, :]
+        ok(lib.npl_matmul(C.byref(ta), C.byref(tb), C.byref(tcm), C.c_float(1.0),
+                          C.c_float(1.0), None))
+        ok(lib.npl_relu(C.byref(tcm), C.byref(tcm), None))
+        ok(lib.npl_layer_norm(C.byref(tcm), C.byref(lnp), C.byref(ty), None))
+
+    sec = timed(big) * (8192 / ms_)
+    out["gemm_relu_layer_norm"] = {
+        "ms_full_workload": round(sec * 1e3, 2),
+        "TFLOP/s (GEMM flops)": round(2.0 * 8192 * 4096 * 16384 / sec / 1e12, 5),
+        "sample": f"{ms_} of 8192 rows, scaled"}
+    out["cores"] = cores
+    return out
+
+
+def _reference_cpu_timed(ref_lib, steps, warmup, rows=False):
     lib = C.CDLL(str(ref_lib))
     nb.bind(lib, nb.NPL_SIGNATURES)
     cores = os.cpu_count() or 1
@@ -208,7 +329,8 @@ def _reference_cpu_timed(ref_lib, steps, warmup):
     sample = (f"full workload (32 images), {len(times)} timed steps, median; reference "
               f"npl_conv2d_bn_activation (conv only) + npl_batch_norm + npl_relu, "
               f"num_threads={cores}, OpenBLAS {cores} threads")
-    return CONV_FLOPS / med / 1e12, cores, sample, med
+    return (CONV_FLOPS / med / 1e12, cores, sample, med,
+            _reference_cpu_rows(lib, cores) if rows else None)
 
 
 # ---------------------------------------------------------------------------
@@ -732,7 +854,7 @@ def main():
             print(json.dumps({"impl": "reference",
                               "unavailable": "oracle/_ref/libnpl_ref.so was not built"}))
             return
-        tflops, cores, sample, med = r
+        tflops, cores, sample, med, _ = r
         print(json.dumps({
             "impl": "reference",
             "metric": "fused conv2d+BN+ReLU TFLOP/s (npl_conv2d_bn_activation, 3xTF32)",
@@ -769,12 +891,14 @@ def main():
                                   "stem": stem_also(lib, local_rank),
                                   "bandwidth": bandwidth_also(lib, local_rank)}
             if world == 1:
-                r = reference_cpu(3, 1)
+                r = reference_cpu(3, 1, rows=not args.no_gemm)
                 if r is not None:
-                    tflops, cores, sample, _ = r
+                    tflops, cores, sample, _, ref_rows = r
                     result["cpu_baseline"] = {"value": round(tflops, 5), "unit": "TFLOP/s",
                                               "cores": cores, "kind": "reference",
                                               "sample": sample}
+                    if ref_rows is not None and "also" in result:
+                        result["also"]["cpu_reference_rows"] = ref_rows
             print(json.dumps(result))
     finally:
         if world > 1:
