@@ -247,6 +247,40 @@ NPL_API int nplk_binary(void *stream, int op, int64_t n, const float *a, const f
 NPL_API int nplk_colshard_relayout(void *stream, int64_t g, int64_t rows, int64_t cols_per_shard,
                            const float *src, float *dst);
 
+/* ---- multi-GPU: peer buffers and the GEMM that writes into them ------------- */
+
+/* Bytes of an inter-process handle of device memory (CUDA IPC). */
+NPL_API size_t nplk_ipc_handle_size(void);
+
+/* Fills `handle` (nplk_ipc_handle_size() bytes) for the allocation holding
+ * dev_ptr and *offset with dev_ptr's byte offset inside it. */
+NPL_API int nplk_ipc_get_handle(const void *dev_ptr, void *handle, uint64_t *offset);
+
+/* Maps another process's allocation (a handle and offset from
+ * nplk_ipc_get_handle) into this process; *dev_ptr receives the address of the
+ * byte at `offset`. Peer access over NVLink is enabled as needed. */
+NPL_API int nplk_ipc_open_handle(const void *handle, uint64_t offset, void **dev_ptr);
+
+/* Unmaps a pointer returned by nplk_ipc_open_handle with the same offset. */
+NPL_API int nplk_ipc_close_handle(void *dev_ptr, uint64_t offset);
+
+/* Column-sharded GEMM fused with its all-gather (replaces nplk_gemm followed by
+ * an all-gather of the column blocks and nplk_colshard_relayout). This rank
+ * computes its block act(alpha * A[M,K] @ B[K,N_local] + bias[N_local]) and the
+ * epilogue stores every output element into each of the n_dst (<= 8) row-major
+ * [M][ldc] buffers dst[0..n_dst) -- this GPU's C and the other ranks' C mapped
+ * with nplk_ipc_open_handle -- at columns col_offset .. col_offset + N_local, so
+ * the exchange crosses NVLink tile by tile while the GEMM runs and every rank
+ * ends with the whole row-major C once all ranks' kernels have completed. `dst`
+ * is a host array of device addresses valid on the current device. beta is 0
+ * (C is not read); other arguments as nplk_gemm. */
+NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
+                                float alpha, const float *A, int64_t lda, const float *B,
+                                int64_t ldb, const float *bias, int act, float act_alpha,
+                                float *const *dst, int n_dst, int64_t col_offset, int64_t ldc,
+                                unsigned flags, void *workspace, size_t workspace_bytes,
+                                int *status);
+
 /* ---- status ----------------------------------------------------------------- */
 
 /* Reads (and clears) the library's per-device kernel status word; 0 = ok.

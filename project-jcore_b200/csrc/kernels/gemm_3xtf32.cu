@@ -54,6 +54,12 @@ struct GemmParams {
   float act_alpha;
   int one_pass;
   int *status;
+  // nplk_gemm_allgather: every output is stored to each of dst[0..n_dst) at
+  // column dst_col + col (row pitch ldc); n_dst = 0 stores to C as nplk_gemm.
+  float *dst[8];
+  int n_dst;
+  int dst_vec;  // 16-byte stores allowed into every dst
+  int64_t dst_col;
 };
 
 // Tile order: groups of 8 M-blocks sweep all N-blocks, so the CTAs resident at
@@ -88,7 +94,31 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
       for (int j = 0; j < 32; ++j) w[j] = 0u;
     }
     const int col0 = nb * BN + c0;
-    if (r < p.M && col0 < p.N) {
+    if (r < p.M && col0 < p.N && p.n_dst > 0) {
+      // Fused exchange: bias and activation, then the same values to every
+      // destination buffer (this GPU's and the peers' over NVLink).
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float o = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
+        if (p.bias && col0 + j < p.N) o += p.bias[col0 + j];
+        out[j] = apply_act(o, p.act, p.act_alpha);
+      }
+      const int64_t off = static_cast<int64_t>(r) * p.ldc + p.dst_col + col0;
+      for (int d = 0; d < p.n_dst; ++d) {
+        float *drow = p.dst[d] + off;
+        if (p.dst_vec && col0 + 32 <= p.N) {
+          float4 *d4 = reinterpret_cast<float4 *>(drow);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            d4[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) drow[j] = out[j];
+        }
+      }
+    } else if (r < p.M && col0 < p.N) {
       float *crow = p.C + static_cast<int64_t>(r) * p.ldc;
       float out[32];
 #pragma unroll
@@ -616,34 +646,28 @@ extern "C" size_t nplk_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return g.a_bytes + g.b_bytes;
 }
 
-extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float alpha,
-                         const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
-                         float *C, int64_t ldc, const float *bias, int act, float act_alpha,
-                         unsigned flags, void *workspace, size_t workspace_bytes,
-                         int *status) {
-  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return kErrInvalidArg;
-  if (lda < K || ldb < N || ldc < N) return kErrInvalidArg;
+namespace nplk {
+namespace {
+
+// Validates the common arguments and runs the GEMM with `prm` (whose epilogue
+// fields the caller has set) in the operand form the flags and workspace
+// select.
+int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, int64_t lda,
+             const float *B, int64_t ldb, GemmParams prm, unsigned flags, void *workspace,
+             size_t workspace_bytes, int *status) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return kErrInvalidArg;
+  if (lda < K || ldb < N) return kErrInvalidArg;
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
     return kErrUnsupported;
   const GemmPlan g = plan_gemm(M, N, K);
   if (!status) status = device_status_word();
   if (!status) return kErrInternal;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-
-  GemmParams prm{};
   prm.M = static_cast<int>(M);
   prm.N = static_cast<int>(N);
   prm.K = static_cast<int>(K);
   prm.m_blocks = static_cast<int>(g.m_blocks);
   prm.n_blocks = static_cast<int>(g.n_blocks);
   prm.k_blocks = static_cast<int>(g.kp / kGemmBK);
-  prm.alpha = alpha;
-  prm.beta = beta;
-  prm.C = C;
-  prm.ldc = ldc;
-  prm.bias = bias;
-  prm.act = act;
-  prm.act_alpha = act_alpha;
   prm.one_pass = (flags & NPLK_GEMM_TF32_FAST) ? 1 : 0;
   prm.status = status;
 
@@ -663,7 +687,7 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
     return launch_gemm_raw<64>(s, g, A, lda, B, ldb, prm);
   }
 
-  if (!workspace || workspace_bytes < g.a_bytes + g.b_bytes) return kErrInvalidArg;
+  if (!have_ws) return kErrInvalidArg;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kErrInvalidArg;
   float *a_split = static_cast<float *>(workspace);
   float *b_split = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + g.a_bytes);
@@ -677,4 +701,54 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
   if (rc) return rc;
   if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm);
   return launch_gemm<64>(s, g, a_split, b_split, prm);
+}
+
+}  // namespace
+}  // namespace nplk
+
+extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float alpha,
+                         const float *A, int64_t lda, const float *B, int64_t ldb, float beta,
+                         float *C, int64_t ldc, const float *bias, int act, float act_alpha,
+                         unsigned flags, void *workspace, size_t workspace_bytes,
+                         int *status) {
+  if (!C || ldc < N) return kErrInvalidArg;
+  GemmParams prm{};
+  prm.alpha = alpha;
+  prm.beta = beta;
+  prm.C = C;
+  prm.ldc = ldc;
+  prm.bias = bias;
+  prm.act = act;
+  prm.act_alpha = act_alpha;
+  return gemm_run(static_cast<cudaStream_t>(stream), M, N, K, A, lda, B, ldb, prm, flags,
+                  workspace, workspace_bytes, status);
+}
+
+extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
+                                   float alpha, const float *A, int64_t lda, const float *B,
+                                   int64_t ldb, const float *bias, int act, float act_alpha,
+                                   float *const *dst, int n_dst, int64_t col_offset, int64_t ldc,
+                                   unsigned flags, void *workspace, size_t workspace_bytes,
+                                   int *status) {
+  if (!dst || n_dst < 1 || n_dst > 8 || col_offset < 0 || ldc < col_offset + N_local)
+    return kErrInvalidArg;
+  GemmParams prm{};
+  prm.alpha = alpha;
+  prm.beta = 0.0f;
+  prm.C = nullptr;
+  prm.ldc = ldc;
+  prm.bias = bias;
+  prm.act = act;
+  prm.act_alpha = act_alpha;
+  prm.n_dst = n_dst;
+  prm.dst_col = col_offset;
+  bool vec = N_local % 4 == 0 && ldc % 4 == 0 && col_offset % 4 == 0;
+  for (int d = 0; d < n_dst; ++d) {
+    if (!dst[d]) return kErrInvalidArg;
+    prm.dst[d] = dst[d];
+    vec = vec && (reinterpret_cast<uintptr_t>(dst[d]) & 15u) == 0;
+  }
+  prm.dst_vec = vec ? 1 : 0;
+  return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, flags,
+                  workspace, workspace_bytes, status);
 }

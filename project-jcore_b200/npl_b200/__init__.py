@@ -188,6 +188,13 @@ NPLK_SIGNATURES = {
     "nplk_global_avg_pool": (C.c_int, [_VP, _I64, _I64, _VP, _VP]),
     "nplk_binary": (C.c_int, [_VP, C.c_int, _I64, _VP, _VP, _VP, C.c_int, _I64, _I64]),
     "nplk_colshard_relayout": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP]),
+    "nplk_ipc_handle_size": (C.c_size_t, []),
+    "nplk_ipc_get_handle": (C.c_int, [_VP, _VP, _P(C.c_uint64)]),
+    "nplk_ipc_open_handle": (C.c_int, [_VP, C.c_uint64, _P(C.c_void_p)]),
+    "nplk_ipc_close_handle": (C.c_int, [_VP, C.c_uint64]),
+    "nplk_gemm_allgather": (C.c_int, [_VP, _I64, _I64, _I64, _F, _VP, _I64, _VP, _I64, _VP,
+                                      C.c_int, _F, _P(C.c_void_p), C.c_int, _I64, _I64,
+                                      C.c_uint, _VP, C.c_size_t, _VP]),
     "nplk_read_status": (C.c_int, [_VP]),
     "nplk_take_launch_count": (C.c_uint64, []),
 }

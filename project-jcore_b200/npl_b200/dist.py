@@ -4,10 +4,13 @@ Two partitionings, following the reference's workloads:
   * convolutions shard by batch: every rank runs npl_conv2d_bn_activation on its
     own images; there is no data exchange (``batch_shard``);
   * the large GEMM shards B and C by column blocks: rank r computes
-    C[:, r*N/g:(r+1)*N/g] = A @ B[:, r*N/g:(r+1)*N/g] (+ bias) with A replicated,
-    then the blocks are all-gathered ([g][M][N/g], one NCCL collective) and
-    rewritten to row-major [M][N] by the relayout kernel
-    (``column_sharded_gemm``).
+    C[:, r*N/g:(r+1)*N/g] = A @ B[:, r*N/g:(r+1)*N/g] (+ bias) with A replicated.
+    Fused form (``PeerBuffers`` + ``column_sharded_gemm_fused``): every rank
+    holds a full row-major C whose address the others map (CUDA IPC), and the
+    GEMM's epilogue stores each output tile into all ranks' C over NVLink
+    (nplk_gemm_allgather) -- no separate collective, no relayout. Unfused form
+    (``column_sharded_gemm``): the blocks are all-gathered ([g][M][N/g], one
+    NCCL collective) and rewritten to row-major [M][N] by the relayout kernel.
 """
 from __future__ import annotations
 
@@ -112,3 +115,83 @@ def column_sharded_gemm(A, B, bias=None, world: int = 1, rank: int = 0, group=No
     if not gather:
         return local
     return gather_column_blocks(local, world, group)
+
+
+class PeerBuffers:
+    """Every rank's copy of one device tensor, mapped into every rank.
+
+    Collective: all ranks construct it together with same-shaped tensors. Each
+    rank exports a CUDA IPC handle of its tensor (nplk_ipc_get_handle), the
+    handles are all-gathered over the process group, and each rank opens the
+    others' (nplk_ipc_open_handle). ``ptrs[r]`` is rank r's tensor as seen
+    from this rank (this rank's own entry is the tensor itself). close() --
+    also collective -- unmaps them; the tensors must outlive it."""
+
+    def __init__(self, tensor, world: int, rank: int, group=None):
+        import torch
+        import torch.distributed as dist
+        from . import load
+
+        self.lib = load()
+        self.tensor = tensor
+        self.world, self.rank, self.group = world, rank, group
+        size = int(self.lib.nplk_ipc_handle_size())
+        handle = (C.c_uint8 * size)()
+        offset = C.c_uint64(0)
+        rc = self.lib.nplk_ipc_get_handle(C.c_void_p(tensor.data_ptr()), handle, C.byref(offset))
+        if rc != 0:
+            raise RuntimeError(f"nplk_ipc_get_handle failed: {rc}")
+        mine = (bytes(handle), int(offset.value))
+        allh = [None] * world
+        dist.all_gather_object(allh, mine, group=group)
+        self.ptrs, self._opened = [], []
+        for r, (h, off) in enumerate(allh):
+            if r == rank:
+                self.ptrs.append(tensor.data_ptr())
+                continue
+            hb = (C.c_uint8 * size).from_buffer_copy(h)
+            p = C.c_void_p()
+            rc = self.lib.nplk_ipc_open_handle(hb, off, C.byref(p))
+            if rc != 0:
+                raise RuntimeError(f"nplk_ipc_open_handle(rank {r}) failed: {rc}")
+            self.ptrs.append(p.value)
+            self._opened.append((p.value, off))
+        torch.cuda.synchronize(tensor.device)
+
+    def close(self):
+        import torch.distributed as dist
+
+        dist.barrier(group=self.group)  # no rank still writes into a peer
+        for p, off in self._opened:
+            self.lib.nplk_ipc_close_handle(C.c_void_p(p), off)
+        self._opened = []
+        dist.barrier(group=self.group)
+
+
+def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=None,
+                              act: int = 0):
+    """C = act(A @ B + bias) with B column-sharded, written by every rank
+    straight into every rank's C (``peers.tensor``, row-major [M][N]) by the
+    GEMM epilogue (nplk_gemm_allgather). Asynchronous on the current stream:
+    C is complete on all ranks once every rank's stream has passed this call
+    (synchronise, then barrier)."""
+    import torch
+
+    lib = peers.lib
+    M, K = A.shape
+    N = B.shape[1]
+    c0, c1 = column_block(N, peers.world, peers.rank)
+    w = c1 - c0
+    ws = lib.nplk_gemm_workspace_size(M, w, K)
+    if workspace is None or workspace.numel() * 4 < ws:
+        workspace = torch.empty(ws // 4 + 64, dtype=torch.float32, device=A.device)
+    stream = C.c_void_p(torch.cuda.current_stream(A.device).cuda_stream)
+    dst = (C.c_void_p * peers.world)(*peers.ptrs)
+    b_ptr = B.data_ptr() + c0 * B.element_size()
+    bias_ptr = C.c_void_p(bias.data_ptr() + c0 * bias.element_size()) if bias is not None else None
+    rc = lib.nplk_gemm_allgather(stream, M, w, K, 1.0, C.c_void_p(A.data_ptr()), K,
+                                 C.c_void_p(b_ptr), N, bias_ptr, act, 0.0, dst, peers.world, c0,
+                                 N, 0, C.c_void_p(workspace.data_ptr()), ws, None)
+    if rc != 0:
+        raise RuntimeError(f"nplk_gemm_allgather failed: {rc}")
+    return peers.tensor

@@ -41,3 +41,89 @@ def test_column_sharded_gemm_simulated_4_ranks():
     assert S.normwise_err(full.cpu().numpy(), ref) < 1e-4
     one = nd.column_sharded_gemm(A, B, bias, world=1, rank=0)
     assert S.normwise_err(one.cpu().numpy(), full.cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("g,M,K,w,act,raw", [(4, 300, 200, 96, 0, True), (3, 129, 64, 50, 1, False),
+                                             (2, 64, 4096, 256, 0, False)])
+def test_gemm_allgather_fused_epilogue_simulated(g, M, K, w, act, raw):
+    # The fused GEMM + all-gather on one device: g buffers stand for the g
+    # ranks' C; each "rank" computes its column block and its epilogue stores
+    # the block into all g buffers, which must all end up holding the whole
+    # C = act(A @ B + bias), bit for bit alike.
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator(device="cuda").manual_seed(g * M + w)
+    N = g * w
+    A = torch.randn(M, K, device="cuda", generator=gen)
+    B = torch.randn(K, N, device="cuda", generator=gen) / 10.0
+    bias = torch.randn(N, device="cuda", generator=gen) * 0.1
+    Cs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(g)]
+    dst = (C.c_void_p * g)(*[c.data_ptr() for c in Cs])
+    ws = 0 if raw else lib.nplk_gemm_workspace_size(M, w, K)
+    work = torch.empty(ws // 4 + 64, device="cuda") if ws else None
+    for r in range(g):
+        rc = lib.nplk_gemm_allgather(
+            S.cuda_stream(), M, w, K, 1.0, S.dptr(A), K, C.c_void_p(B.data_ptr() + 4 * r * w), N,
+            C.c_void_p(bias.data_ptr() + 4 * r * w), act, 0.0, dst, g, r * w, N,
+            nb.NPLK_GEMM_RAW_OPERANDS if raw else 0,
+            S.dptr(work) if work is not None else None, ws, None)
+        assert rc == 0, rc
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(S.cuda_stream()) == 0
+    ref = A.double().cpu().numpy() @ B.double().cpu().numpy() + bias.double().cpu().numpy()
+    if act:
+        ref = np.maximum(ref, 0.0)
+    first = Cs[0].cpu().numpy()
+    assert S.normwise_err(first, ref) < 1e-4
+    for c in Cs[1:]:
+        assert np.array_equal(c.cpu().numpy(), first)
+
+
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ipc_rank(rank, world, port, results):
+    import os
+    import torch
+    import torch.distributed as dist
+    from npl_b200 import dist as nd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.cuda.set_device(rank % torch.cuda.device_count())
+        gen = torch.Generator(device="cuda").manual_seed(0)  # the same A, B on every rank
+        M, K, N = 256, 192, world * 128
+        A = torch.randn(M, K, device="cuda", generator=gen)
+        B = torch.randn(K, N, device="cuda", generator=gen) / 10.0
+        bias = torch.randn(N, device="cuda", generator=gen) * 0.1
+        full = torch.full((M, N), float("nan"), device="cuda")
+        peers = nd.PeerBuffers(full, world, rank)
+        nd.column_sharded_gemm_fused(A, B, peers, bias)
+        torch.cuda.synchronize()
+        dist.barrier()  # every rank's blocks have landed in every C
+        ref = A.double().cpu().numpy() @ B.double().cpu().numpy() + bias.double().cpu().numpy()
+        got = full.cpu().numpy()
+        results[rank] = (float(np.isnan(got).sum()), S.normwise_err(got, ref))
+        peers.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gemm_allgather_ipc_two_processes():
+    # Two ranks (their own GPUs when there are two, else both on one): CUDA IPC
+    # handles exchanged over gloo, each rank's GEMM epilogue writing into both
+    # ranks' C.
+    import torch.multiprocessing as mp
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_ipc_rank, args=(world, _free_port(), results), nprocs=world,
+                       start_method="spawn", join=True)
+    assert sorted(results.keys()) == [0, 1]
+    for nan_count, err in results.values():
+        assert nan_count == 0 and err < 1e-4
