@@ -30,6 +30,10 @@ namespace nplk {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 32;
 constexpr int kGemmThreads = 192;
+// Fused-exchange staging per epilogue warp: 32 rows x 32 columns, row pitch 36
+// floats (16-byte aligned rows, conflict-free float4 access); four warps.
+constexpr int kEpiStagePitch = 36;
+constexpr int kEpiStageBytes = 4 * 32 * kEpiStagePitch * 4;
 
 template <int BN>
 struct GemmTraits {
@@ -40,7 +44,7 @@ struct GemmTraits {
   static constexpr int kAccCols = 2 * BN;
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + kEpiStageBytes;
 };
 
 struct GemmParams {
@@ -80,7 +84,7 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_b
 // TMEM: C = alpha*(D[:, :BN] + D[:, BN:]) + beta*C + bias, activation, store.
 template <int BN>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t t_row, int r,
-                                                   int nb, bool vec_ok) {
+                                                   int nb, bool vec_ok, float *stg) {
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
     uint32_t v[32], w[32];
@@ -94,30 +98,50 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
       for (int j = 0; j < 32; ++j) w[j] = 0u;
     }
     const int col0 = nb * BN + c0;
-    if (r < p.M && col0 < p.N && p.n_dst > 0) {
+    if (p.n_dst > 0) {
       // Fused exchange: bias and activation, then the same values to every
-      // destination buffer (this GPU's and the peers' over NVLink).
-      float out[32];
+      // destination buffer (this GPU's and the peers' over NVLink). The warp's
+      // 32 x 32 block goes through shared memory so that each store
+      // instruction writes four whole 128-byte row segments instead of 32
+      // scattered 16-byte pieces (one row per lane).
+      const int lane = threadIdx.x & 31;
+      if (col0 < p.N) {
+        float out[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float o = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
-        if (p.bias && col0 + j < p.N) o += p.bias[col0 + j];
-        out[j] = apply_act(o, p.act, p.act_alpha);
+        for (int j = 0; j < 32; ++j) {
+          float o = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
+          if (p.bias && col0 + j < p.N) o += p.bias[col0 + j];
+          out[j] = apply_act(o, p.act, p.act_alpha);
+        }
+        float4 *s4 = reinterpret_cast<float4 *>(stg + lane * kEpiStagePitch);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          s4[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
       }
-      const int64_t off = static_cast<int64_t>(r) * p.ldc + p.dst_col + col0;
-      for (int d = 0; d < p.n_dst; ++d) {
-        float *drow = p.dst[d] + off;
-        if (p.dst_vec && col0 + 32 <= p.N) {
-          float4 *d4 = reinterpret_cast<float4 *>(drow);
+      __syncwarp();
+      if (col0 < p.N) {
+        const int r0 = r - lane;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            d4[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) drow[j] = out[j];
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3);
+          const int col = col0 + 4 * (lane & 7);
+          const int row = r0 + rr;
+          const float4 val = *reinterpret_cast<const float4 *>(stg + rr * kEpiStagePitch +
+                                                               4 * (lane & 7));
+          if (row < p.M && col < p.N) {
+            const int64_t off = static_cast<int64_t>(row) * p.ldc + p.dst_col + col;
+            if (p.dst_vec && col + 4 <= p.N) {
+              for (int d = 0; d < p.n_dst; ++d)
+                *reinterpret_cast<float4 *>(p.dst[d] + off) = val;
+            } else {
+              const float e[4] = {val.x, val.y, val.z, val.w};
+              for (int d = 0; d < p.n_dst; ++d)
+                for (int k = 0; k < 4 && col + k < p.N; ++k) p.dst[d][off + k] = e[k];
+            }
+          }
         }
       }
+      __syncwarp();  // the next chunk rewrites the staging block
     } else if (r < p.M && col0 < p.N) {
       float *crow = p.C + static_cast<int64_t>(r) * p.ldc;
       float out[32];
@@ -289,6 +313,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
+    float *stg = reinterpret_cast<float *>(smem_b + T::kStages * T::kBStageBytes +
+                                           T::kBarrierBytes) +
+                 (warp - 2) * 32 * kEpiStagePitch;
     const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
                         ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
     int local = 0;
@@ -303,7 +330,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-gemm_epilogue_tile<BN>(p, t_row, r, nb, vec_ok);
+gemm_epilogue_tile<BN>(p, t_row, r, nb, vec_ok, stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -349,7 +376,7 @@ struct RawGemmTraits {
   static constexpr int kTxBytes = kAHalf + kBHalf;  // what TMA writes per stage
   static constexpr int kAccCols = 2 * BN;
   static constexpr int kTmemCols = 2 * kAccCols;
-  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256 + kEpiStageBytes;
 };
 
 __device__ __forceinline__ float tf32_lo_trunc(float x) {
@@ -491,6 +518,8 @@ __global__ void __launch_bounds__(kRawThreads, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
+    float *stg = reinterpret_cast<float *>(smem + T::kStages * T::kStageBytes + 256) +
+                 (warp - 2) * 32 * kEpiStagePitch;
     const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
                         ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
     int local = 0;
@@ -504,7 +533,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-      gemm_epilogue_tile<BN>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok);
+      gemm_epilogue_tile<BN>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok, stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
