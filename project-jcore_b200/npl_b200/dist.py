@@ -153,6 +153,9 @@ class PeerBuffers:
             p = C.c_void_p()
             rc = self.lib.nplk_ipc_open_handle(hb, off, C.byref(p))
             if rc != 0:
+                for q, qoff in self._opened:  # do not leak the mappings made so far
+                    self.lib.nplk_ipc_close_handle(C.c_void_p(q), qoff)
+                self._opened = []
                 raise RuntimeError(f"nplk_ipc_open_handle(rank {r}) failed: {rc}")
             self.ptrs.append(p.value)
             self._opened.append((p.value, off))
