@@ -82,7 +82,7 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_b
 
 // Drains one accumulator tile row (this thread's row r of the tile) from
 // TMEM: C = alpha*(D[:, :BN] + D[:, BN:]) + beta*C + bias, activation, store.
-template <int BN>
+template <int BN, bool kFused>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t t_row, int r,
                                                    int nb, bool vec_ok, float *stg) {
 #pragma unroll 1
@@ -98,7 +98,7 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
       for (int j = 0; j < 32; ++j) w[j] = 0u;
     }
     const int col0 = nb * BN + c0;
-    if (p.n_dst > 0) {
+    if constexpr (kFused) {
       // Fused exchange: bias and activation, then the same values to every
       // destination buffer (this GPU's and the peers' over NVLink). The warp's
       // 32 x 32 block goes through shared memory so that each store
@@ -188,7 +188,9 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
   }
 }
 
-template <int BN>
+// kFused: the fused-exchange epilogue (nplk_gemm_allgather); a separate
+// instantiation keeps the plain GEMM's code as it was.
+template <int BN, bool kFused>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
@@ -330,7 +332,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-gemm_epilogue_tile<BN>(p, t_row, r, nb, vec_ok, stg);
+gemm_epilogue_tile<BN, kFused>(p, t_row, r, nb, vec_ok, stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -384,7 +386,7 @@ __device__ __forceinline__ float tf32_lo_trunc(float x) {
   return fabsf(x) == CUDART_INF_F ? 0.0f : x - hi;
 }
 
-template <int BN>
+template <int BN, bool kFused>
 __global__ void __launch_bounds__(kRawThreads, 1)
     gemm_3xtf32_raw_kernel(const __grid_constant__ CUtensorMap map_a,
                            const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
@@ -533,7 +535,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-      gemm_epilogue_tile<BN>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok, stg);
+      gemm_epilogue_tile<BN, kFused>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok, stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -619,13 +621,23 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
   rc = encode_tmap_2d_f32_sw128(&map_b, b_split, g.kp, g.n_blocks * 2 * BN, g.kp * 4, kGemmBK,
                                 2 * BN);
   if (rc) return rc;
-  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN>),
-                          T::kSmemBytes);
-  if (rc) return rc;
   const int64_t tiles = g.m_blocks * g.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  return launch_programmatic(gemm_3xtf32_kernel<BN>, dim3(grid), dim3(kGemmThreads),
-                             T::kSmemBytes, stream, map_a, map_b, prm);
+  // The epilogue staging block only for the fused exchange: with programmatic
+  // dependent launch the GEMM's CTAs become resident while the split kernels
+  // still run, and 18 KB less shared memory leaves those room on the SM.
+  if (prm.n_dst > 0) {
+    rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN, true>),
+                             T::kSmemBytes);
+    if (rc) return rc;
+    return launch_programmatic(gemm_3xtf32_kernel<BN, true>, dim3(grid), dim3(kGemmThreads),
+                               T::kSmemBytes, stream, map_a, map_b, prm);
+  }
+  const int smem = T::kSmemBytes - kEpiStageBytes;
+  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN, false>), smem);
+  if (rc) return rc;
+  return launch_programmatic(gemm_3xtf32_kernel<BN, false>, dim3(grid), dim3(kGemmThreads), smem,
+                             stream, map_a, map_b, prm);
 }
 
 // The raw-operand form applies when TMA can read A and B in place: 16-byte
@@ -645,12 +657,18 @@ int launch_gemm_raw(cudaStream_t stream, const GemmPlan &g, const float *A, int6
   if (rc) return rc;
   rc = encode_tmap_2d_f32_sw128_atom32(&map_b, B, prm.N, prm.K, ldb * 4, 32, kGemmBK);
   if (rc) return rc;
-  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN>),
-                           T::kSmemBytes);
-  if (rc) return rc;
   const int64_t tiles = g.m_blocks * g.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  gemm_3xtf32_raw_kernel<BN><<<grid, kRawThreads, T::kSmemBytes, stream>>>(map_a, map_b, prm);
+  const bool fused = prm.n_dst > 0;  // staging block only then, as launch_gemm
+  const int smem = T::kSmemBytes - (fused ? 0 : kEpiStageBytes);
+  const void *fn = fused ? reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, true>)
+                         : reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, false>);
+  rc = ensure_dynamic_smem(fn, smem);
+  if (rc) return rc;
+  if (fused)
+    gemm_3xtf32_raw_kernel<BN, true><<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm);
+  else
+    gemm_3xtf32_raw_kernel<BN, false><<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm);
   count_launch();
   return launch_result();
 }
