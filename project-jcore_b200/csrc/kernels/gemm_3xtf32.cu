@@ -58,13 +58,19 @@ struct GemmParams {
   float act_alpha;
   int one_pass;
   int *status;
-  // nplk_gemm_allgather: every output is stored to each of dst[0..n_dst) at
-  // column dst_col + col (row pitch ldc); n_dst = 0 stores to C as nplk_gemm.
+};
+
+// nplk_gemm_allgather: every output is stored to each of dst[0..n_dst) at
+// column dst_col + col (row pitch GemmParams::ldc). A kernel parameter of the
+// fused instantiation only: the plain GEMM's parameter block keeps its size
+// (with these 88 bytes in it the 1024^3 GEMM kernel ran 45 us against 37).
+struct GemmDst {
   float *dst[8];
   int n_dst;
   int dst_vec;  // 16-byte stores allowed into every dst
   int64_t dst_col;
 };
+struct GemmNoDst {};
 
 // Tile order: groups of 8 M-blocks sweep all N-blocks, so the CTAs resident at
 // one time share A row-blocks and B column-blocks in L2.
@@ -82,9 +88,10 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_b
 
 // Drains one accumulator tile row (this thread's row r of the tile) from
 // TMEM: C = alpha*(D[:, :BN] + D[:, BN:]) + beta*C + bias, activation, store.
-template <int BN, bool kFused>
-__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t t_row, int r,
-                                                   int nb, bool vec_ok, float *stg) {
+template <int BN, bool kFused, class Dst>
+__device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Dst &pd,
+                                                   uint32_t t_row, int r, int nb, bool vec_ok,
+                                                   float *stg) {
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
     uint32_t v[32], w[32];
@@ -129,14 +136,14 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
           const float4 val = *reinterpret_cast<const float4 *>(stg + rr * kEpiStagePitch +
                                                                4 * (lane & 7));
           if (row < p.M && col < p.N) {
-            const int64_t off = static_cast<int64_t>(row) * p.ldc + p.dst_col + col;
-            if (p.dst_vec && col + 4 <= p.N) {
-              for (int d = 0; d < p.n_dst; ++d)
-                *reinterpret_cast<float4 *>(p.dst[d] + off) = val;
+            const int64_t off = static_cast<int64_t>(row) * p.ldc + pd.dst_col + col;
+            if (pd.dst_vec && col + 4 <= p.N) {
+              for (int d = 0; d < pd.n_dst; ++d)
+                *reinterpret_cast<float4 *>(pd.dst[d] + off) = val;
             } else {
               const float e[4] = {val.x, val.y, val.z, val.w};
-              for (int d = 0; d < p.n_dst; ++d)
-                for (int k = 0; k < 4 && col + k < p.N; ++k) p.dst[d][off + k] = e[k];
+              for (int d = 0; d < pd.n_dst; ++d)
+                for (int k = 0; k < 4 && col + k < p.N; ++k) pd.dst[d][off + k] = e[k];
             }
           }
         }
@@ -190,10 +197,11 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, uint32_t
 
 // kFused: the fused-exchange epilogue (nplk_gemm_allgather); a separate
 // instantiation keeps the plain GEMM's code as it was.
-template <int BN, bool kFused>
+template <int BN, bool kFused, class Dst>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_a,
-                       const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+                       const __grid_constant__ CUtensorMap map_b, const GemmParams p,
+                       const __grid_constant__ Dst pd) {
   using T = GemmTraits<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -332,7 +340,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-gemm_epilogue_tile<BN, kFused>(p, t_row, r, nb, vec_ok, stg);
+gemm_epilogue_tile<BN, kFused>(p, pd, t_row, r, nb, vec_ok, stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -386,10 +394,11 @@ __device__ __forceinline__ float tf32_lo_trunc(float x) {
   return fabsf(x) == CUDART_INF_F ? 0.0f : x - hi;
 }
 
-template <int BN, bool kFused>
+template <int BN, bool kFused, class Dst>
 __global__ void __launch_bounds__(kRawThreads, 1)
     gemm_3xtf32_raw_kernel(const __grid_constant__ CUtensorMap map_a,
-                           const __grid_constant__ CUtensorMap map_b, const GemmParams p) {
+                           const __grid_constant__ CUtensorMap map_b, const GemmParams p,
+                           const __grid_constant__ Dst pd) {
   using T = RawGemmTraits<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -535,7 +544,8 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-      gemm_epilogue_tile<BN, kFused>(p, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok, stg);
+      gemm_epilogue_tile<BN, kFused>(p, pd, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok,
+                                     stg);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -612,7 +622,7 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K) {
 
 template <int BN>
 int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
-                const float *b_split, GemmParams prm) {
+                const float *b_split, const GemmParams &prm, const GemmDst *pd) {
   using T = GemmTraits<BN>;
   CUtensorMap map_a, map_b;
   int rc = encode_tmap_2d_f32_sw128(&map_a, a_split, g.kp, g.m_blocks * 2 * kGemmBM, g.kp * 4,
@@ -626,18 +636,19 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
   // The epilogue staging block only for the fused exchange: with programmatic
   // dependent launch the GEMM's CTAs become resident while the split kernels
   // still run, and 18 KB less shared memory leaves those room on the SM.
-  if (prm.n_dst > 0) {
-    rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN, true>),
-                             T::kSmemBytes);
+  if (pd) {
+    auto *fn = gemm_3xtf32_kernel<BN, true, GemmDst>;
+    rc = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), T::kSmemBytes);
     if (rc) return rc;
-    return launch_programmatic(gemm_3xtf32_kernel<BN, true>, dim3(grid), dim3(kGemmThreads),
-                               T::kSmemBytes, stream, map_a, map_b, prm);
+    return launch_programmatic(fn, dim3(grid), dim3(kGemmThreads), T::kSmemBytes, stream, map_a,
+                               map_b, prm, *pd);
   }
+  auto *fn = gemm_3xtf32_kernel<BN, false, GemmNoDst>;
   const int smem = T::kSmemBytes - kEpiStageBytes;
-  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(gemm_3xtf32_kernel<BN, false>), smem);
+  rc = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), smem);
   if (rc) return rc;
-  return launch_programmatic(gemm_3xtf32_kernel<BN, false>, dim3(grid), dim3(kGemmThreads), smem,
-                             stream, map_a, map_b, prm);
+  return launch_programmatic(fn, dim3(grid), dim3(kGemmThreads), smem, stream, map_a, map_b, prm,
+                             GemmNoDst{});
 }
 
 // The raw-operand form applies when TMA can read A and B in place: 16-byte
@@ -650,7 +661,7 @@ bool gemm_raw_ok(const float *A, int64_t lda, const float *B, int64_t ldb, int64
 
 template <int BN>
 int launch_gemm_raw(cudaStream_t stream, const GemmPlan &g, const float *A, int64_t lda,
-                    const float *B, int64_t ldb, GemmParams prm) {
+                    const float *B, int64_t ldb, const GemmParams &prm, const GemmDst *pd) {
   using T = RawGemmTraits<BN>;
   CUtensorMap map_a, map_b;
   int rc = encode_tmap_2d_f32_sw128(&map_a, A, prm.K, prm.M, lda * 4, kGemmBK, kGemmBM);
@@ -659,16 +670,19 @@ int launch_gemm_raw(cudaStream_t stream, const GemmPlan &g, const float *A, int6
   if (rc) return rc;
   const int64_t tiles = g.m_blocks * g.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  const bool fused = prm.n_dst > 0;  // staging block only then, as launch_gemm
+  const bool fused = pd != nullptr;  // staging block only then, as launch_gemm
   const int smem = T::kSmemBytes - (fused ? 0 : kEpiStageBytes);
-  const void *fn = fused ? reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, true>)
-                         : reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, false>);
+  const void *fn =
+      fused ? reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, true, GemmDst>)
+            : reinterpret_cast<const void *>(gemm_3xtf32_raw_kernel<BN, false, GemmNoDst>);
   rc = ensure_dynamic_smem(fn, smem);
   if (rc) return rc;
   if (fused)
-    gemm_3xtf32_raw_kernel<BN, true><<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm);
+    gemm_3xtf32_raw_kernel<BN, true, GemmDst>
+        <<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm, *pd);
   else
-    gemm_3xtf32_raw_kernel<BN, false><<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm);
+    gemm_3xtf32_raw_kernel<BN, false, GemmNoDst>
+        <<<grid, kRawThreads, smem, stream>>>(map_a, map_b, prm, GemmNoDst{});
   count_launch();
   return launch_result();
 }
@@ -698,10 +712,10 @@ namespace {
 
 // Validates the common arguments and runs the GEMM with `prm` (whose epilogue
 // fields the caller has set) in the operand form the flags and workspace
-// select.
+// select; `pd` non-null selects the fused exchange epilogue.
 int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, int64_t lda,
-             const float *B, int64_t ldb, GemmParams prm, unsigned flags, void *workspace,
-             size_t workspace_bytes, int *status) {
+             const float *B, int64_t ldb, GemmParams prm, const GemmDst *pd, unsigned flags,
+             void *workspace, size_t workspace_bytes, int *status) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return kErrInvalidArg;
   if (lda < K || ldb < N) return kErrInvalidArg;
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
@@ -730,8 +744,8 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   const bool raw = (flags & NPLK_GEMM_RAW_OPERANDS) ||
                    (!have_ws && raw_ok && !(flags & NPLK_GEMM_SPLIT_OPERANDS));
   if (raw) {
-    if (g.bn == 128) return launch_gemm_raw<128>(s, g, A, lda, B, ldb, prm);
-    return launch_gemm_raw<64>(s, g, A, lda, B, ldb, prm);
+    if (g.bn == 128) return launch_gemm_raw<128>(s, g, A, lda, B, ldb, prm, pd);
+    return launch_gemm_raw<64>(s, g, A, lda, B, ldb, prm, pd);
   }
 
   if (!have_ws) return kErrInvalidArg;
@@ -746,8 +760,8 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   // the splits before its first load.
   rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn, true);
   if (rc) return rc;
-  if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm);
-  return launch_gemm<64>(s, g, a_split, b_split, prm);
+  if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm, pd);
+  return launch_gemm<64>(s, g, a_split, b_split, prm, pd);
 }
 
 }  // namespace
@@ -767,8 +781,8 @@ extern "C" int nplk_gemm(void *stream, int64_t M, int64_t N, int64_t K, float al
   prm.bias = bias;
   prm.act = act;
   prm.act_alpha = act_alpha;
-  return gemm_run(static_cast<cudaStream_t>(stream), M, N, K, A, lda, B, ldb, prm, flags,
-                  workspace, workspace_bytes, status);
+  return gemm_run(static_cast<cudaStream_t>(stream), M, N, K, A, lda, B, ldb, prm, nullptr,
+                  flags, workspace, workspace_bytes, status);
 }
 
 extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
@@ -787,15 +801,16 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
   prm.bias = bias;
   prm.act = act;
   prm.act_alpha = act_alpha;
-  prm.n_dst = n_dst;
-  prm.dst_col = col_offset;
+  GemmDst pd{};
+  pd.n_dst = n_dst;
+  pd.dst_col = col_offset;
   bool vec = N_local % 4 == 0 && ldc % 4 == 0 && col_offset % 4 == 0;
   for (int d = 0; d < n_dst; ++d) {
     if (!dst[d]) return kErrInvalidArg;
-    prm.dst[d] = dst[d];
+    pd.dst[d] = dst[d];
     vec = vec && (reinterpret_cast<uintptr_t>(dst[d]) & 15u) == 0;
   }
-  prm.dst_vec = vec ? 1 : 0;
-  return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, flags,
-                  workspace, workspace_bytes, status);
+  pd.dst_vec = vec ? 1 : 0;
+  return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, &pd,
+                  flags, workspace, workspace_bytes, status);
 }
