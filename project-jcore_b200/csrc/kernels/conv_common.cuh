@@ -54,6 +54,28 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// One lane's 32 outputs of an accumulator chunk: channel j of the chunk goes
+// to y[j * plane]. The constants come from shared memory through pointers the
+// compiler knows to be shared (align_smem_1024), and the restrict qualifiers
+// tell it that the stores to y do not touch them, so it may load later
+// channels' constants before storing earlier outputs.
+template <int kAct, bool kFull>
+__device__ __forceinline__ void conv_store_chunk(float *__restrict__ y, int64_t plane,
+                                                 const float4 *__restrict__ q,
+                                                 const float *__restrict__ beta,
+                                                 const uint32_t (&v)[32], const uint32_t (&w)[32],
+                                                 int nco, int act, float act_alpha) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (!kFull && j >= nco) continue;
+    const float4 c = q[j];
+    float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + c.x;
+    // Without BN the constants are mean 0, gamma 1, inv_std 1, beta 0.
+    t = c.z * (t - c.y) * c.w + beta[j];
+    y[j * plane] = epilogue_act<kAct>(t, act, act_alpha);
+  }
+}
+
 // Drains one finished accumulator tile (GEMM rows mb*128.., channels
 // nb*BNC..) to NCHW, skipping rows that are not output pixels:
 // out = act(gamma*((D[:, :BNC] + D[:, BNC:] + bias) - mean)*inv_std + beta).
@@ -102,25 +124,13 @@ __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t
     tmem_wait_ld2(v, w);
     const int co0 = nb * BNC + c0;
     if (valid) {
-      if (co0 + 32 <= p.Cout) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float4 q = ep_s[c0 + j];
-          float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
-          // Without BN the constants are mean 0, gamma 1, inv_std 1, beta 0.
-          t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
-          yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (co0 + j >= p.Cout) continue;
-          const float4 q = ep_s[c0 + j];
-          float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + q.x;
-          t = q.z * (t - q.y) * q.w + ep_beta_s[c0 + j];
-          yb[static_cast<int64_t>(co0 + j) * p.HoWo] = epilogue_act<kAct>(t, p.act, p.act_alpha);
-        }
-      }
+      float *yc = yb + static_cast<int64_t>(co0) * p.HoWo;
+      if (co0 + 32 <= p.Cout)
+        conv_store_chunk<kAct, true>(yc, p.HoWo, ep_s + c0, ep_beta_s + c0, v, w, 32, p.act,
+                                     p.act_alpha);
+      else
+        conv_store_chunk<kAct, false>(yc, p.HoWo, ep_s + c0, ep_beta_s + c0, v, w,
+                                      p.Cout - co0, p.act, p.act_alpha);
     }
   }
   return true;

@@ -85,8 +85,7 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
     conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
   using T = ConvTraits<BNC>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint8_t *smem_a = smem;
   uint8_t *smem_b = smem + T::kStages * T::kAStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem_b + T::kStages * T::kBStageBytes);

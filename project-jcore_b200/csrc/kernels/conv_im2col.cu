@@ -156,8 +156,7 @@ __global__ void __launch_bounds__(ConvTmaTraits<BNC>::kThreads, 1)
   constexpr int P = T::kPipes;
   constexpr int S = T::kStages;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint8_t *bars = smem + P * S * T::kStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(bars);  // [P][S]
   uint64_t *empty = full + P * S;                        // [P][S]

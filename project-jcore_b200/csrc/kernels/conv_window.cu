@@ -91,8 +91,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   constexpr int WS = T::kWinSlots;
   constexpr int BS = T::kBSlots;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint8_t *bslots = smem + T::kWinAreaBytes;
   uint8_t *bars = smem + T::kPipeBytes;
   uint64_t *win_full = reinterpret_cast<uint64_t *>(bars);  // [P][WS] raw window landed

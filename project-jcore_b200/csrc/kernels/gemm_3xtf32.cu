@@ -204,8 +204,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                        const __grid_constant__ Dst pd) {
   using T = GemmTraits<BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint8_t *smem_a = smem;
   uint8_t *smem_b = smem + T::kStages * T::kAStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem_b + T::kStages * T::kBStageBytes);
@@ -401,8 +400,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
                            const __grid_constant__ Dst pd) {
   using T = RawGemmTraits<BN>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023u));
+  uint8_t *smem = align_smem_1024(smem_raw);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + T::kStages * T::kStageBytes);
   uint64_t *lo_ready = full + T::kStages;
   uint64_t *empty = lo_ready + T::kStages;

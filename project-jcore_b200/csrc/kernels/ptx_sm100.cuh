@@ -35,6 +35,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The first 1024-byte boundary at or after `raw` (the dynamic shared-memory
+// array), reached by offsetting `raw` itself: the compiler then keeps the
+// result and every pointer derived from it in the shared address space, so
+// accesses through them are ld/st.shared. Aligning the address as an integer
+// instead makes them generic accesses; in the conv epilogue those constant
+// loads could not be scheduled ahead of its global stores, one load round
+// trip per output channel (3.5 vs 1.3 kcycles per 32 channels measured).
+__device__ __forceinline__ uint8_t *align_smem_1024(uint8_t *raw) {
+  return raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
+}
+
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
