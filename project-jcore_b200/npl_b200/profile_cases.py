@@ -125,7 +125,8 @@ CASES = {"conv": case_conv,
          "conv_s2": lambda: case_conv(cout=128, stride=2),
          "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
          "layernorm": case_layernorm, "pool": case_pool,
-         "gemm_raw": lambda: case_gemm(raw=True)}
+         "gemm_raw": lambda: case_gemm(raw=True),
+         "gemm_1024": lambda: case_gemm(m=1024, n=1024, k=1024)}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else "conv"
