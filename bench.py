@@ -482,7 +482,7 @@ def run_b200(args, rank, world, local_rank):
             "scaling": "weak",
             "vs_baseline": None,
             "dtype": "f32 (3xTF32 tensor-core products, fp32 accumulate)",
-            "data": "synthetic (seeded: BASELINE distributions)",
+            "data": "synthetic (seeded; the benchmark workload's shapes and value distributions)",
             "config": {
                 "workload": WORKLOAD,
                 "per_gpu_batch": N_IMG,
@@ -900,7 +900,7 @@ def main():
             "value": round(tflops, 5), "unit": "TFLOP/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded: BASELINE distributions)",
+            "dtype": "f32", "data": "synthetic (seeded; the benchmark workload's shapes and value distributions)",
             "config": {"workload": WORKLOAD, "per_gpu_batch": N_IMG,
                        "global_batch": N_IMG, "parallelism": "host CPU (reference build)"},
             "cpu_baseline": {"value": round(tflops, 5), "unit": "TFLOP/s", "cores": cores,

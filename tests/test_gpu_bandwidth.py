@@ -1,6 +1,6 @@
 """Parity of the bandwidth-bound NPL primitives (depthwise conv, batch norm,
 activations, global average pool, softmax, layer norm, pooling, add/mul) with
-the oracle: full-size BASELINE shapes plus ragged and edge cases. Integer-like
+the oracle: the benchmark workloads at full size plus ragged and edge cases. Integer-like
 work (max pooling, ReLU, depthwise with the reference's FMA order) is checked
 bit for bit; reductions and transcendentals within 1e-5 normwise."""
 import ctypes as C
@@ -19,7 +19,7 @@ def run(lib, name, *args):
     assert rc == 0, (name, lib.npl_strerror(rc))
 
 
-def test_bandwidth_chain_config4_full():
+def test_bandwidth_chain_256x512x14x14_full():
     # depthwise 3x3 pad 1 -> BN -> ReLU -> GAP -> softmax over 512 channels,
     # N=256, C=512, 14x14, inputs N(0,1), dw weights N(0,0.3).
     lib = S.gpu_lib()
@@ -150,7 +150,7 @@ def test_softmax_axes():
         nb.NPL_ERR_INVALID_ARG
 
 
-def test_layer_norm_golden_and_config5_rows():
+def test_layer_norm_golden_and_8192x16384_rows():
     lib = S.gpu_lib()
     g = dict(np.load(S.GOLDEN / "layer_norm.npz"))
     h = S.HostTensors(lib)

@@ -84,7 +84,7 @@ def test_conv_bn_relu_golden():
     assert st.was_fused == 1
 
 
-def test_conv_bn_relu_config2_full():
+def test_conv_bn_relu_3x3_n32_c64_56x56_full():
     # ResNet 3x3 layer: N=32, Cin=64, 56x56, Cout=64, stride 1, pad 1, no bias.
     lib = S.gpu_lib()
     rng = S.rng(0)
@@ -93,7 +93,7 @@ def test_conv_bn_relu_config2_full():
     bn = bn_params(64, rng)
     y, st = fused_host(lib, x, w, bn, nb.NPL_ACT_RELU, pad=(1, 1))
     err = S.normwise_err(y, oracle_fused(x, w, bn, 1, pad=(1, 1)))
-    print(f"config2 normwise err {err:.3e}")
+    print(f"3x3 N=32 64->64 56x56 normwise err {err:.3e}")
     assert err < TOL
 
 

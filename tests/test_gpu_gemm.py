@@ -76,7 +76,7 @@ def test_matmul_golden():
     assert S.normwise_err(c, g["c"]) < TOL
 
 
-def test_matmul_config1_vs_oracle_and_reference():
+def test_matmul_1024_vs_oracle_and_reference():
     # npl_matmul fp32 1024^3, A and B uniform[-1,1] from seed 0.
     lib = S.gpu_lib()
     rng = S.rng(0)
@@ -128,9 +128,9 @@ def test_matmul_batched():
         assert S.normwise_err(c[i], S.o_sgemm(a[i], b[i])) < TOL
 
 
-def test_gemm_config5_device_sampled_rows():
+def test_gemm_8192x4096x16384_device_sampled_rows():
     # npl_matmul fp32 [8192x4096] @ [4096x16384] with the per-column bias fed
-    # through beta=1 on a pre-filled C (BASELINE large-GEMM case); parity on a
+    # through beta=1 on a pre-filled C (the large-GEMM benchmark case); parity on a
     # seeded sample of rows against an fp64 product.
     import torch
     lib = S.gpu_lib()

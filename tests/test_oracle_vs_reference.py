@@ -1,6 +1,6 @@
 """Cross-checks the C oracle against the reference's own NPL code
 (oracle/_ref/libnpl_ref.so, built from the reference sources) on seeded
-random inputs with the BASELINE shape families at reduced sizes, plus edge
+random inputs with the benchmark workloads' shape families at reduced sizes, plus edge
 cases. Skipped where the reference build is absent."""
 import ctypes as C
 
