@@ -131,3 +131,35 @@ def test_kernel_abi_argument_checks(lib):
     assert lib.nplk_softmax(None, 0, 4, 1, None, None) == nb.NPL_ERR_INVALID_ARG
     assert lib.nplk_pool2d(None, 1, 1, 4, 4, 2, 2, 2, 2, 0, 0, 2, 2, 5, 0, None, None) == \
         nb.NPL_ERR_INVALID_ARG
+
+
+def test_multi_gpu_entry_points_argument_checks(lib):
+    # The fused GEMM all-gather and the IPC calls reject bad arguments before
+    # any device work.
+    assert lib.nplk_ipc_handle_size() == 64  # cudaIpcMemHandle_t
+    h = (C.c_uint8 * 64)()
+    off = C.c_uint64(0)
+    p = C.c_void_p()
+    assert lib.nplk_ipc_get_handle(None, h, C.byref(off)) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_ipc_get_handle(C.c_void_p(0x1000), None, C.byref(off)) == \
+        nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_ipc_get_handle(C.c_void_p(0x1000), h, None) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_ipc_open_handle(None, 0, C.byref(p)) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_ipc_open_handle(h, 0, None) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_ipc_close_handle(None, 0) == nb.NPL_ERR_INVALID_ARG
+
+    fake = C.c_void_p(0x1000)  # never dereferenced: every call below fails its checks
+
+    def allgather(dst, n_dst, col_offset, ldc, n_local=64):
+        return lib.nplk_gemm_allgather(None, 128, n_local, 64, 1.0, fake, 64, fake, 128, None, 0,
+                                       0.0, dst, n_dst, col_offset, ldc, 0, None, 0, None)
+
+    two = (C.c_void_p * 2)(0x1000, 0x2000)
+    nine = (C.c_void_p * 9)(*([0x1000] * 9))
+    with_null = (C.c_void_p * 2)(0x1000, None)
+    assert allgather(None, 2, 0, 128) == nb.NPL_ERR_INVALID_ARG          # no destinations
+    assert allgather(two, 0, 0, 128) == nb.NPL_ERR_INVALID_ARG           # n_dst < 1
+    assert allgather(nine, 9, 0, 128) == nb.NPL_ERR_INVALID_ARG          # n_dst > 8
+    assert allgather(two, 2, -4, 128) == nb.NPL_ERR_INVALID_ARG          # negative column
+    assert allgather(two, 2, 96, 128) == nb.NPL_ERR_INVALID_ARG          # block past ldc
+    assert allgather(with_null, 2, 0, 128) == nb.NPL_ERR_INVALID_ARG     # a null destination
