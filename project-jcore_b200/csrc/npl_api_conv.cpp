@@ -121,9 +121,13 @@ int run_conv_pipelined(const nplk_conv_geom_t &g, const npl_tensor_t *input,
   const int chunks = pipeline_chunks(n, sizes);
   int per = 0;
   for (int c = 0; c < chunks; ++c) per = sizes[c] > per ? sizes[c] : per;
+  npl::Call call;  // binds the library's device before the lanes are made on it
+  if (call.status()) return call.finish(nullptr, 0, 0, nullptr);
   npl::CopyLanes *lanes = npl::copy_lanes(2 * static_cast<size_t>(chunks) + 2);
-  if (!lanes) return NPL_ERR_INTERNAL;
-  npl::Call call;
+  if (!lanes) {
+    call.fail(NPL_ERR_INTERNAL);
+    return call.finish(nullptr, 0, 0, nullptr);
+  }
   const float *w = call.input(weights->data, w_elems * 4);
   const float *b = bias ? call.input(bias->data, co * 4) : nullptr;
   const float *mean = nullptr, *var = nullptr, *gamma = nullptr, *beta = nullptr;

@@ -97,6 +97,12 @@ thread_local ThreadLanes t_lanes;
 
 CopyLanes *copy_lanes(size_t events) {
   const int dev = state().device;
+  // Streams and events belong to the current device: make it the library's
+  // (a thread's first call may come with another device current).
+  if (cudaSetDevice(dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
   if (t_lanes.device != dev) {
     t_lanes.release();
     if (cudaStreamCreateWithFlags(&t_lanes.lanes.in, cudaStreamNonBlocking) != cudaSuccess ||

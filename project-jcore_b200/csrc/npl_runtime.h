@@ -108,6 +108,7 @@ struct CopyLanes {
   std::vector<cudaEvent_t> events;
 };
 // The calling thread's lanes with at least `events` events, or NULL on error.
+// Leaves the library's device current.
 CopyLanes *copy_lanes(size_t events);
 // True for page-locked host memory (asynchronous copies overlap compute).
 bool is_pinned_host(const void *p);
