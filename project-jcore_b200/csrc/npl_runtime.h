@@ -18,7 +18,7 @@ namespace npl {
 
 struct State {
   std::mutex mu;
-  bool initialized = false;
+  std::atomic<bool> initialized{false};  // read without the mutex by calls on any thread
   npl_config_t config{};
   int device = 0;
   cudaStream_t stream = nullptr;
