@@ -233,13 +233,17 @@ NPL_API int nplk_pool2d(void *stream, int64_t n, int64_t c, int64_t h, int64_t w
  * (ExecuteGlobalAvgPooling, npl_pooling.cpp:317-385). */
 NPL_API int nplk_global_avg_pool(void *stream, int64_t planes, int64_t hw, const float *x, float *y);
 
-/* Elementwise binary ops over n elements: op 0 = add, 1 = mul.
- * b_mode: 0 = same shape, 1 = b is a scalar, 2 = a is a scalar,
- * 3 = b is per-channel [C] over NCHW planes of `inner` elements. */
+/* Elementwise binary ops over n elements: op 0 = add, 1 = mul (npl_add /
+ * npl_mul, npl_tensor_ops.cpp:440-662). b_mode: 0 = same shape, 1 = b is a
+ * scalar, 2 = a is a scalar, 3 = b is per-channel [C] over NCHW planes of
+ * `inner` elements. */
 NPL_API int nplk_binary(void *stream, int op, int64_t n, const float *a, const float *b, float *c,
                 int b_mode, int64_t channels, int64_t inner);
 
 /* ---- multi-GPU helpers ------------------------------------------------------ */
+/* The reference has no multi-device path: these serve npl_matmul's product
+ * (npl_tensor_ops.cpp:115-153 -> ExecuteMatMulDirect :217-311) computed as
+ * column blocks on several GPUs, one process per GPU. */
 
 /* Column-shard relayout after an all-gather: src is [g][rows][cols_per_shard]
  * (shard-major, as an all-gather of per-rank C blocks delivers it); dst is
@@ -249,7 +253,8 @@ NPL_API int nplk_colshard_relayout(void *stream, int64_t g, int64_t rows, int64_
 
 /* ---- multi-GPU: peer buffers and the GEMM that writes into them ------------- */
 
-/* Bytes of an inter-process handle of device memory (CUDA IPC). */
+/* Bytes of an inter-process handle of device memory (CUDA IPC). The nplk_ipc_*
+ * calls have no reference counterpart (the reference runs in one process). */
 NPL_API size_t nplk_ipc_handle_size(void);
 
 /* Fills `handle` (nplk_ipc_handle_size() bytes) for the allocation holding
@@ -284,7 +289,8 @@ NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_
 /* ---- status ----------------------------------------------------------------- */
 
 /* Reads (and clears) the library's per-device kernel status word; 0 = ok.
- * Synchronises `stream`. */
+ * Synchronises `stream`. No reference counterpart: the reference's kernels
+ * cannot time out, its errors are the return codes (neural_primitives.h:52-59). */
 NPL_API int nplk_read_status(void *stream);
 
 /* Number of library kernels launched on this thread since the last call
