@@ -1,8 +1,10 @@
 """Host logic of PeerBuffers (npl_b200.dist) on CPU ranks (gloo, world size
 3): the handle exchange, the order of the mapped pointers, close() unmapping
 every peer it mapped, and a failed nplk_ipc_open_handle unmapping the peers
-already opened before it raises. The library's IPC entry points are replaced
-by a fake whose handles name the exporting rank, so no GPU is involved."""
+already opened before it raises; and the arguments column_sharded_gemm_fused
+passes to nplk_gemm_allgather on each rank. The library's entry points are
+replaced by fakes (IPC handles that name the exporting rank, a GEMM that
+records its call), so no GPU is involved."""
 import ctypes as C
 import os
 import socket
@@ -120,3 +122,54 @@ def test_peer_buffers_unmaps_opened_peers_when_an_open_fails():
         assert status == "ok" and ptrs[r] == own
         assert [q for q, _ in opened] == [q for q in range(world) if q != r]
         assert closed == []  # close() is collective; not called once a rank failed
+
+
+class RecordingGemmLib:
+    """nplk_gemm_workspace_size and nplk_gemm_allgather, recording the call."""
+
+    def __init__(self):
+        self.calls = []
+
+    def nplk_gemm_workspace_size(self, m, n, k):
+        return 4 * (m * k + n * k) * 2
+
+    def nplk_gemm_allgather(self, *args):
+        self.calls.append(args)
+        return 0
+
+
+class _Peers:
+    def __init__(self, lib, tensor, world, rank, ptrs):
+        self.lib, self.tensor, self.world, self.rank, self.ptrs = lib, tensor, world, rank, ptrs
+
+
+def test_column_sharded_gemm_fused_arguments(monkeypatch):
+    # Each rank passes its column block of B and bias, every rank's C as the
+    # destinations, its column offset and the full row pitch.
+    from npl_b200 import dist as nd
+
+    class _Stream:
+        cuda_stream = 0
+
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda *a, **k: _Stream())
+    M, K, N, world = 64, 48, 96, 3
+    A = torch.zeros(M, K)
+    B = torch.zeros(K, N)
+    bias = torch.zeros(N)
+    ptrs = [0x100000, 0x200000, 0x300000]
+    for rank in range(world):
+        lib = RecordingGemmLib()
+        C_full = torch.zeros(M, N)
+        out = nd.column_sharded_gemm_fused(A, B, _Peers(lib, C_full, world, rank, ptrs), bias,
+                                           act=1)
+        assert out is C_full and len(lib.calls) == 1
+        (stream, m, w, k, alpha, a, lda, b, ldb, bias_p, act, act_alpha, dst, n_dst, col0, ldc,
+         flags, work, ws, status) = lib.calls[0]
+        c0, c1 = nd.column_block(N, world, rank)
+        assert (m, w, k, lda, ldb, ldc, n_dst, col0) == (M, c1 - c0, K, K, N, N, world, c0)
+        assert alpha == 1.0 and act == 1 and flags == 0 and status is None
+        assert a.value == A.data_ptr()
+        assert b.value == B.data_ptr() + 4 * c0
+        assert bias_p.value == bias.data_ptr() + 4 * c0
+        assert [dst[i] for i in range(world)] == ptrs
+        assert ws == lib.nplk_gemm_workspace_size(M, c1 - c0, K) and work.value is not None
