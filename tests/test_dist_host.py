@@ -1,4 +1,4 @@
-"""Host logic of the multi-GPU paths on CPU ranks (gloo, world size 2): the
+"""Host logic of the multi-GPU paths on CPU ranks (gloo, world sizes 2 and 4): the
 batch and column shard plans and the gather order of the column-sharded GEMM.
 Each rank computes its column block with the oracle GEMM (the stand-in for
 nplk_gemm on CPU), the blocks are all-gathered over gloo and laid out with a
@@ -61,11 +61,11 @@ def _rank_main(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_column_sharded_gemm_gather_gloo_world2():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_column_sharded_gemm_gather_gloo(world):
     mgr = mp.get_context("spawn").Manager()
     results = mgr.dict()
     mp.start_processes(_rank_main, args=(world, _free_port(), results), nprocs=world,
                        start_method="spawn", join=True)
-    assert sorted(results.keys()) == [0, 1]
+    assert sorted(results.keys()) == list(range(world))
     assert max(results.values()) < 1e-6
