@@ -50,6 +50,7 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO / "project-jcore_b200"))
 import npl_b200 as nb  # noqa: E402
+from npl_b200 import workloads  # noqa: E402
 
 N_IMG, C_IN, HW_IN, C_OUT, KSZ = 32, 64, 56, 64, 3
 CONV_FLOPS = 2.0 * N_IMG * C_OUT * C_IN * HW_IN * HW_IN * KSZ * KSZ
@@ -572,13 +573,10 @@ def bandwidth_also(lib, local_rank, reps=10):
     chain_bytes = (nx * 8 + w.numel() * 4) + nx * 8 + nx * 8 + (nx * 4 + n * c * 4) + n * c * 8
 
     def chain():
-        rcs = (lib.nplk_depthwise_conv2d(s, C.byref(g), p(x), p(w), None, p(y)),
-               lib.nplk_batch_norm_infer(s, n, c, hw * hw, p(y), p(y2), p(bn[0]), p(bn[1]),
-                                         p(bn[2]), p(bn[3]), 1e-5),
-               lib.nplk_activation(s, nx, p(y2), p(y2), 1, 0.0, 0),
-               lib.nplk_global_avg_pool(s, n * c, hw * hw, p(y2), p(gap)),
-               lib.nplk_softmax(s, n, c, 1, p(gap), p(sm_out)))
-        return max(abs(r) for r in rcs)
+        # the same function tests/test_gpu_workloads.py checks against the
+        # reference's CPU chain
+        return abs(workloads.bandwidth_chain(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], y, y2,
+                                             gap, sm_out))
 
     cases.append(("chain depthwise->BN->ReLU->GAP->softmax [256,512,14,14]", chain_bytes,
                   chain))
@@ -661,14 +659,13 @@ def gemm_also(lib, args, local_rank):
     Y = torch.empty_like(Cm)
     pipe_ms, ln_ms = [], []
     for _ in range(n):
-        Cm.copy_(bias.expand(GEMM_M, GEMM_N))
+        workloads.fill_bias_rows(Cm, bias)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
-        r = lib.nplk_gemm(sptr, GEMM_M, GEMM_N, GEMM_K, 1.0, p(A), GEMM_K, p(B), GEMM_N, 1.0,
-                          p(Cm), GEMM_N, None, nb.NPL_ACT_RELU, 0.0, 0, p(work), ws, None)
-        assert r == 0, r
-        e1.record(stream)
-        r = lib.nplk_layer_norm(sptr, GEMM_M, GEMM_N, p(Cm), p(Y), None, None, 1e-5)
+        # the same function tests/test_gpu_workloads.py checks against the
+        # reference's npl_matmul (beta 1) -> npl_relu -> npl_layer_norm
+        r = workloads.gemm_bias_relu_layer_norm(lib, sptr, A, B, Cm, Y, work, ws,
+                                                between=lambda: e1.record(stream))
         assert r == 0, r
         e2.record(stream)
         torch.cuda.synchronize()
@@ -773,6 +770,117 @@ def gemm1024_also(lib, local_rank, reps=20):
             "TFLOP/s": round(2 * m ** 3 / (ms / 1e3) / 1e12, 2), "normwise_err": err}
 
 
+def strong_scaling_also(lib, rank, world, local_rank, reps=10):
+    """The stated batches split over the ranks (strong scaling, no collective):
+    the 3x3 layer's 32 images, the stem's 128 and the bandwidth chain's 256,
+    each rank taking a contiguous block of batch_shard(N, world, rank) images
+    (inputs resident on its GPU, weights replicated). Per rank: median CUDA-
+    event time of `reps` runs with L2 flushed before each; the line's time is
+    the max over ranks and its throughput the whole batch's work over that
+    time. With more than one rank, rank 0 also times the whole batch on its
+    own GPU, so each line carries its speed-up and efficiency against one GPU.
+    The loop each rank runs is ExecuteConvDirect's ParallelFor over N*Cout
+    (npl_convolution.cpp:267-342) cut along N."""
+    import torch
+    import torch.distributed as dist
+    from npl_b200 import dist as nd
+
+    dev = torch.device("cuda", local_rank)
+    s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    flush = make_l2_flush(dev)
+
+    def timed(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            flush()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        if lib.nplk_read_status(s) != 0:
+            raise RuntimeError("a kernel reported a pipeline timeout")
+        return statistics.median(ts)
+
+    def conv_case(n, c, hw, cout, k, stride, pad, x_lo, x_hi, pool):
+        gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+        x = torch.rand(n, c, hw, hw, device=dev, generator=gen) * (x_hi - x_lo) + x_lo
+        wgen = torch.Generator(device=dev).manual_seed(7)  # replicated weights
+        w = torch.randn(cout, c, k, k, device=dev, generator=wgen) * (2.0 / (c * k * k)) ** 0.5
+        bn = [torch.rand(cout, device=dev, generator=wgen) + 0.5 for _ in range(4)]
+        g = nb.conv_geom(n, c, hw, hw, cout, k, k, stride, pad)
+        y = torch.empty(n, cout, g.h_out, g.w_out, device=dev)
+        ws = lib.nplk_conv_workspace_size(C.byref(g))
+        work = torch.empty(ws // 4 + 64, device=dev)
+        ho = g.h_out
+        pooled = torch.empty(n, cout, (ho + 2 - 3) // 2 + 1, (ho + 2 - 3) // 2 + 1,
+                             device=dev) if pool else None
+
+        def fn():
+            r = lib.nplk_conv2d_fused(s, C.byref(g), p(x), p(w), None, p(bn[0]), p(bn[1]),
+                                      p(bn[2]), p(bn[3]), 1e-5, nb.NPL_ACT_RELU, 0.0, p(y),
+                                      p(work), ws, None)
+            assert r == 0, r
+            if pool:
+                po = pooled.shape[-1]
+                r = lib.nplk_pool2d(s, n, cout, ho, ho, 3, 3, 2, 2, 1, 1, po, po, 0, 0, p(y),
+                                    p(pooled))
+                assert r == 0, r
+        return fn
+
+    def chain_case(n):
+        gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+        x = torch.randn(n, 512, 14, 14, device=dev, generator=gen)
+        wgen = torch.Generator(device=dev).manual_seed(8)
+        w = torch.randn(512, 1, 3, 3, device=dev, generator=wgen) * 0.3
+        bn = [torch.rand(512, device=dev, generator=wgen) + 0.5 for _ in range(4)]
+        y, y2 = torch.empty_like(x), torch.empty_like(x)
+        gap, probs = torch.empty(n, 512, device=dev), torch.empty(n, 512, device=dev)
+
+        def fn():
+            r = workloads.bandwidth_chain(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], y, y2, gap,
+                                          probs)
+            assert r == 0, r
+        return fn
+
+    cases = [
+        ("conv3x3 N=32 C=64 56x56 (+BN+ReLU)", 32, "TFLOP/s",
+         lambda n: 2.0 * n * 64 * 64 * 56 * 56 * 9 / 1e12,
+         lambda n: conv_case(n, 64, 56, 64, 3, 1, 1, 0.0, 1.0, False)),
+        ("stem conv7x7/s2 N=128 (+BN+ReLU) + max pool 3x3/s2", 128, "TFLOP/s (conv flops)",
+         lambda n: 2.0 * n * 64 * 3 * 112 * 112 * 49 / 1e12,
+         lambda n: conv_case(n, 3, 224, 64, 7, 2, 3, -1.0, 1.0, True)),
+        ("depthwise->BN->ReLU->GAP->softmax N=256 C=512 14x14", 256, "GB/s",
+         lambda n: n * 720914432 / 256 / 1e9,
+         lambda n: chain_case(n)),
+    ]
+    out = {}
+    for name, n_total, unit, work_of, make in cases:
+        b0, b1 = nd.batch_shard(n_total, world, rank)
+        ms = timed(make(b1 - b0))
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+        entry = {"global_batch": n_total, "per_gpu_batch": b1 - b0, "ms": round(ms_max, 4),
+                 "value": round(work_of(n_total) / (ms_max / 1e3), 2), "unit": unit}
+        if world > 1 and rank == 0:
+            ms1 = timed(make(n_total))
+            entry["one_gpu_ms"] = round(ms1, 4)
+            entry["speedup"] = round(ms1 / ms_max, 3)
+            entry["efficiency"] = round(ms1 / ms_max / world, 3)
+        if world > 1:
+            dist.barrier()
+        out[name] = entry
+        torch.cuda.empty_cache()
+    return {"scaling": "strong (the stated batch split over the GPUs, no collective)",
+            "time": "per-rank median CUDA-event time, L2 flushed before each run, max over "
+                    "ranks", "cases": out}
+
+
 def gemm_dist(args, rank, world, local_rank):
     """Column-sharded large GEMM on `world` GPUs: each rank computes its block
     of C = A @ B + bias (A replicated) and every rank ends with the whole
@@ -855,6 +963,27 @@ def gemm_dist(args, rank, world, local_rank):
     finally:
         peers.close()
     fm = tf.item()
+    # Every rank's whole C against a one-GPU GEMM of the same inputs on this
+    # rank (same k order and epilogue, so bit-identical is expected), for
+    # both exchange forms.
+    ws_full = lib.nplk_gemm_workspace_size(GEMM_M, GEMM_N, GEMM_K)
+    work_full = torch.empty(ws_full // 4 + 64, device=dev)
+    c_ref = torch.empty(GEMM_M, GEMM_N, device=dev)
+    r = lib.nplk_gemm(C.c_void_p(stream.cuda_stream), GEMM_M, GEMM_N, GEMM_K, 1.0,
+                      C.c_void_p(A.data_ptr()), GEMM_K, C.c_void_p(B.data_ptr()), GEMM_N, 0.0,
+                      C.c_void_p(c_ref.data_ptr()), GEMM_N, C.c_void_p(bias.data_ptr()), 0, 0.0,
+                      0, C.c_void_p(work_full.data_ptr()), ws_full, None)
+    assert r == 0, r
+    torch.cuda.synchronize()
+    same = torch.tensor([int(torch.equal(full_f, c_ref)), int(torch.equal(full, c_ref))],
+                        device=dev, dtype=torch.int64)
+    diff = torch.tensor([((full_f - c_ref).abs().max() / c_ref.abs().max()).item()],
+                        device=dev, dtype=torch.float64)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    dist.all_reduce(diff, op=dist.ReduceOp.MAX)
+    del work_full, c_ref
+    torch.cuda.empty_cache()
+    egress = (world - 1) * GEMM_M * (GEMM_N // world) * 4  # bytes each rank stores to peers
     return {"workload": f"npl_matmul fp32 [8192x4096]@[4096x16384] + bias, B/C column-sharded "
                         f"over {world} GPUs",
             "gemm_only_value": round(GEMM_FLOPS / (gm / 1e3) / 1e12, 2),
@@ -862,11 +991,16 @@ def gemm_dist(args, rank, world, local_rank):
             "end_to_end": "fused (below): every rank holds the whole row-major C",
             "gemm_ms": round(gm, 4),
             "nccl": {"gemm_allgather_relayout_ms": round(tm, 4),
+                     "c_identical_all_ranks": bool(same[1].item()),
                      "value": round(GEMM_FLOPS / (tm / 1e3) / 1e12, 2),
                      "step": "GEMM, then NCCL all-gather of the [g][M][N/g] blocks, then the "
                              "relayout kernel"},
             "fused": {"ms": round(fm, 4), "value": round(GEMM_FLOPS / (fm / 1e3) / 1e12, 2),
                       "normwise_err_sampled_rows": ferr,
+                      "c_identical_all_ranks": bool(same[0].item()),
+                      "c_max_normwise_diff_all_ranks": float(diff.item()),
+                      "peer_egress_bytes_per_rank": egress,
+                      "peer_egress_GB/s_per_rank": round(egress / (fm / 1e3) / 1e9, 1),
                       "step": "nplk_gemm_allgather: the GEMM epilogue stores every tile into "
                               "all ranks' C over NVLink (CUDA IPC peer pointers)"},
             "normwise_err_sampled_rows": err}
@@ -923,12 +1057,15 @@ def main():
             gd = gemm_dist(args, rank, world, local_rank)
             if rank == 0:
                 result["also"] = {"gemm_column_sharded": gd}
+        strong = strong_scaling_also(lib, rank, world, local_rank)
+        if rank == 0:
+            result.setdefault("also", {})["conv_strong_scaling"] = strong
         if rank == 0:
             if world == 1 and not args.no_gemm:
-                result["also"] = {"gemm": gemm_also(lib, args, local_rank),
-                                  "gemm_1024": gemm1024_also(lib, local_rank),
-                                  "stem": stem_also(lib, local_rank),
-                                  "bandwidth": bandwidth_also(lib, local_rank)}
+                result["also"].update({"gemm": gemm_also(lib, args, local_rank),
+                                       "gemm_1024": gemm1024_also(lib, local_rank),
+                                       "stem": stem_also(lib, local_rank),
+                                       "bandwidth": bandwidth_also(lib, local_rank)})
             if world == 1:
                 r = reference_cpu(3, 1, rows=not args.no_gemm)
                 if r is not None:

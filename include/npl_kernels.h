@@ -174,8 +174,11 @@ NPL_API int nplk_conv2d_run_staged(void *stream, const nplk_conv_geom_t *g, int 
  * GPU loading the library keeps until exit; larger geometries are rejected
  * with NPL_ERR_UNSUPPORTED. The first call on a device looks up that array's
  * address, so it should precede any stream capture. All calls on a device
- * share the array: calls that overlap on the GPU race. status may be NULL
- * (an internal word is used and cleared by each call). Allocates nothing. */
+ * share the array: calls that overlap on the GPU race. status may be NULL:
+ * a word beside the array is then cleared by each call and receives any
+ * timeout code; nplk_read_status() reads and clears it (and allocates
+ * nothing), so read it after each call whose outcome matters. Allocates
+ * nothing. */
 NPL_API int nplk_conv2d_fused_noalloc(void *stream, const nplk_conv_geom_t *g, const float *x,
                                       const float *w, const float *bias, const float *bn_mean,
                                       const float *bn_var, const float *bn_gamma,
@@ -288,14 +291,37 @@ NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_
 
 /* ---- status ----------------------------------------------------------------- */
 
-/* Reads (and clears) the library's per-device kernel status word; 0 = ok.
- * Synchronises `stream`. No reference counterpart: the reference's kernels
+/* Reads (and clears) the library's per-device kernel status word and the
+ * status word of nplk_conv2d_fused_noalloc; returns the first non-zero code,
+ * 0 = ok. Synchronises `stream`. Allocates nothing: a word that no kernel
+ * can have written yet is not created. No reference counterpart: the reference's kernels
  * cannot time out, its errors are the return codes (neural_primitives.h:52-59). */
 NPL_API int nplk_read_status(void *stream);
 
 /* Number of library kernels launched on this thread since the last call
  * (resets the counter). */
 NPL_API uint64_t nplk_take_launch_count(void);
+
+/* ---- fault injection (tests of the failure paths) --------------------------- */
+/* No reference counterpart: the reference's CPU loops cannot time out or run
+ * out of device memory. Both hooks are off unless armed. */
+
+#define NPLK_DEBUG_GEMM 1        /* the tcgen05 GEMM kernels (split and raw forms) */
+#define NPLK_DEBUG_CONV_WINDOW 2 /* the window conv kernels (gather and plane forms) */
+
+/* Arms the next launch of one kernel family, from any thread, to exercise its
+ * bounded-wait timeout: that launch's MMA issuer waits on a barrier nothing
+ * arrives on, with a limit of stall_us microseconds (<= 60 s) instead of the
+ * kernels' 4 s. On expiry the kernel records 102 (MMA wait expired) in its
+ * status word, every role leaves on the CTA's abort flag, copies in flight
+ * land, TMEM is freed and the kernel returns; its outputs are undefined.
+ * stall_us = 0 disarms. Returns 0 or NPL_ERR_INVALID_ARG. */
+NPL_API int nplk_debug_arm_wait_timeout(int which, uint32_t stall_us);
+
+/* The next `count` device allocations made by npl_* calls (staging of host
+ * tensors and per-call scratch) fail as if the device were out of memory;
+ * count = 0 disarms. Returns the number still armed before this call. */
+NPL_API int nplk_debug_fail_next_allocations(int count);
 
 #ifdef __cplusplus
 }

@@ -37,6 +37,7 @@ struct ConvParams {
   int cout_pad;
   int act;
   float act_alpha;
+  uint32_t stall_us;  // fault injection: 0 except on an armed launch (injected_stall)
   int *status;
 };
 

@@ -21,6 +21,11 @@
 //   * Set-up: the first call on each device looks up the array's device
 //     address (cudaGetSymbolAddress) with that device current. That first
 //     call should therefore come before any stream capture.
+//   * Status: with status == NULL the kernels report a bounded-wait timeout
+//     to a word kept beside the array; nplk_read_status() reads and clears it
+//     (together with the library's other status word) without allocating.
+//     Each call clears that word before its kernels run, so read it after
+//     every call whose outcome matters.
 //   * Sharing: all calls on a device use the same array, which keeps whatever
 //     the last call wrote. Each call rewrites every byte it later reads, and
 //     clears the status word it uses, before its kernels run. Calls whose
@@ -79,6 +84,14 @@ int noalloc_setup(void **scratch, int **status) {
 }
 
 }  // namespace
+
+int *noalloc_status_word_if_set_up() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  return g_status_ptr[dev];
+}
+
 }  // namespace nplk
 
 using namespace nplk;

@@ -101,7 +101,8 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   uint64_t *b_empty = b_full + BS;                           // [BS], one arrival per pipeline
   uint64_t *acc_full = b_empty + BS;                         // [P * kAccPerPipe]
   uint64_t *acc_empty = acc_full + P * T::kAccPerPipe;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + P * T::kAccPerPipe);
+  uint64_t *never = acc_empty + P * T::kAccPerPipe;  // never arrived on (injected_stall)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(never + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   float4 *ep_s = reinterpret_cast<float4 *>(bars + T::kBarrierBytes);
   float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(never, 1);
     *abort_flag = 0;
     fence_mbar_init();
     if (!kGather) tma_prefetch_desc(&map_x);
@@ -237,7 +239,8 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
       int ws = 0, bs = 0;
       uint32_t wph = 0, bph = 0;
       int jj = 0;
-      for (int tile = blockIdx.x + pipe * gridDim.x; tile < num_tiles;
+      const bool go = injected_stall(never, p.stall_us, abort_flag, p.status);
+      for (int tile = blockIdx.x + pipe * gridDim.x; go && tile < num_tiles;
            tile += P * gridDim.x, ++jj) {
         const int acc = pipe * T::kAccPerPipe + (jj & 1);
         const uint32_t acc_phase = (jj >> 1) & 1;
@@ -533,6 +536,7 @@ int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp,
   prm.Wv = wv;
   prm.Mv = static_cast<int>(mv);
   prm.m_blocks = static_cast<int>(ceil_div(mv, kConvBM));
+  prm.stall_us = take_armed_stall(NPLK_DEBUG_CONV_WINDOW);
   CUtensorMap mx, mw;
   int rc = kOk;
   if (gather) {

@@ -57,6 +57,7 @@ struct GemmParams {
   int act;
   float act_alpha;
   int one_pass;
+  uint32_t stall_us;  // fault injection: 0 except on an armed launch (injected_stall)
   int *status;
 };
 
@@ -211,7 +212,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *empty = full + T::kStages;
   uint64_t *acc_full = empty + T::kStages;
   uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *never = acc_empty + 2;  // never arrived on (injected_stall)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(never + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -226,6 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(never, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&map_a);
@@ -248,6 +251,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       griddep_wait();  // the split operands come from the kernels just before
       int stage = 0;
       uint32_t phase = 0;
+      uint32_t pending = 0;  // stages that received a copy, with its phase
+      uint32_t pending_phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         int mb, nb;
         gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
@@ -260,13 +265,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       mb * 2 * kGemmBM);
           tma_load_2d(&map_b, &full[stage], smem_b + stage * T::kBStageBytes, kb * kGemmBK,
                       nb * 2 * BN);
+          pending |= 1u << stage;
+          pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == T::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-    producer_done:;
+    producer_done:
+      // Let the last copy into each stage land before the CTA can exit (they
+      // already have unless the CTA aborted).
+      for (int s2 = 0; s2 < T::kStages; ++s2)
+        if ((pending >> s2) & 1u) mbar_drain(&full[s2], (pending_phase >> s2) & 1u);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -278,7 +289,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const bool go = injected_stall(never, p.stall_us, abort_flag, p.status);
+      for (int tile = blockIdx.x; go && tile < num_tiles; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
@@ -406,7 +418,8 @@ __global__ void __launch_bounds__(kRawThreads, 1)
   uint64_t *empty = lo_ready + T::kStages;
   uint64_t *acc_full = empty + T::kStages;
   uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *never = acc_empty + 2;  // never arrived on (injected_stall)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(never + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -422,6 +435,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], 4);
     }
+    mbar_init(never, 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&map_a);
@@ -480,7 +494,8 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const bool go = injected_stall(never, p.stall_us, abort_flag, p.status);
+      for (int tile = blockIdx.x; go && tile < num_tiles; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
@@ -728,6 +743,7 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   prm.n_blocks = static_cast<int>(g.n_blocks);
   prm.k_blocks = static_cast<int>(g.kp / kGemmBK);
   prm.one_pass = (flags & NPLK_GEMM_TF32_FAST) ? 1 : 0;
+  prm.stall_us = take_armed_stall(NPLK_DEBUG_GEMM);
   prm.status = status;
 
   // Operand form: split (hi/lo copies in the workspace, then the GEMM) when

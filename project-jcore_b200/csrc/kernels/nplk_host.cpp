@@ -31,6 +31,8 @@ int g_sm_count[kMaxDevices];
 std::mutex g_status_mu;
 int *g_status[kMaxDevices];
 thread_local uint64_t t_launches = 0;
+constexpr int kDebugFamilies = 3;  // index = NPLK_DEBUG_* code
+std::atomic<uint32_t> g_armed_stall[kDebugFamilies];
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
@@ -86,6 +88,20 @@ int *device_status_word() {
     g_status[dev] = p;
   }
   return g_status[dev];
+}
+
+int *device_status_word_if_allocated() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  return g_status[dev];
+}
+
+uint32_t take_armed_stall(int which) {
+  if (which <= 0 || which >= kDebugFamilies) return 0u;
+  // Cheap when nothing is armed: a load, no read-modify-write.
+  if (g_armed_stall[which].load(std::memory_order_relaxed) == 0u) return 0u;
+  return g_armed_stall[which].exchange(0u);
 }
 
 void count_launch(uint64_t n) { t_launches += n; }
@@ -170,15 +186,30 @@ int encode_tmap_im2col_nhwc_f32_sw128(CUtensorMap *map, const void *base, uint64
 }  // namespace nplk
 
 extern "C" int nplk_read_status(void *stream) {
-  int *w = nplk::device_status_word();
-  if (!w) return nplk::kErrInternal;
-  int v = 0;
+  // Two words can hold a report: the library's per-device word (kernels
+  // launched with status == NULL) and the word of the no-allocation conv
+  // entry point. Each is read and cleared only if it exists, so reading the
+  // status allocates nothing. The first non-zero code is returned.
+  int *words[2] = {nplk::device_status_word_if_allocated(),
+                   nplk::noalloc_status_word_if_set_up()};
+  int vals[2] = {0, 0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess)
-    return nplk::kErrInternal;
-  if (cudaMemsetAsync(w, 0, sizeof(int), s) != cudaSuccess) return nplk::kErrInternal;
+  for (int i = 0; i < 2; ++i) {
+    if (!words[i]) continue;
+    if (cudaMemcpyAsync(&vals[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, s) !=
+        cudaSuccess)
+      return nplk::kErrInternal;
+    if (cudaMemsetAsync(words[i], 0, sizeof(int), s) != cudaSuccess) return nplk::kErrInternal;
+  }
   if (cudaStreamSynchronize(s) != cudaSuccess) return nplk::kErrInternal;
-  return v;
+  return vals[0] ? vals[0] : vals[1];
+}
+
+extern "C" int nplk_debug_arm_wait_timeout(int which, uint32_t stall_us) {
+  if (which != NPLK_DEBUG_GEMM && which != NPLK_DEBUG_CONV_WINDOW) return nplk::kErrInvalidArg;
+  if (stall_us > 60000000u) return nplk::kErrInvalidArg;  // at most one minute
+  nplk::g_armed_stall[which].store(stall_us);
+  return nplk::kOk;
 }
 
 extern "C" uint64_t nplk_take_launch_count(void) {

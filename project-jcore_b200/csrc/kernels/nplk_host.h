@@ -29,6 +29,19 @@ int sm_count();
 // Device status word of the current device (allocated on first use).
 int *device_status_word();
 
+// The same word if it has been allocated on the current device, else NULL
+// (nothing has reported to it yet). Never allocates.
+int *device_status_word_if_allocated();
+
+// Status word of the no-allocation conv entry point on the current device if
+// that entry point has been set up there, else NULL. Never allocates.
+int *noalloc_status_word_if_set_up();
+
+// Fault injection (nplk_debug_arm_wait_timeout): the stall, in microseconds,
+// armed for the next launch of kernel family `which` (NPLK_DEBUG_*), which
+// this call consumes; 0 when nothing is armed.
+uint32_t take_armed_stall(int which);
+
 // Counts one library kernel launch on the calling thread.
 void count_launch(uint64_t n = 1);
 

@@ -87,23 +87,43 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t *bar, uint32_t parity
 }
 
 // Waits until the phase with the given parity has completed. Returns false if
-// the CTA was told to abort or if the wait exceeded kWaitLimitNs, in which case
+// the CTA was told to abort or if the wait exceeded limit_ns, in which case
 // `code` is recorded in *status (first error wins) and *abort is raised.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                          int *status, int code) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity,
+                                              volatile int *abort, int *status, int code,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 31u) == 0u) {
       if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort = 1;
         atomicCAS(status, 0, code);
         return false;
       }
     }
   }
+}
+
+// mbar_wait_for with the kernels' standard limit, kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          int *status, int code) {
+  return mbar_wait_for(bar, parity, abort, status, code, kWaitLimitNs);
+}
+
+// Fault injection (nplk_debug_arm_wait_timeout): the MMA issuer of an armed
+// launch first waits, with a limit of `stall_us` microseconds, on `never`, a
+// barrier of the CTA that is initialised and never arrived on. The wait
+// expires through the ordinary timeout path (status code, abort flag), and
+// every other role of the CTA leaves its loop on the abort flag. Returns
+// false when the CTA is aborting; true (at once) when stall_us is 0.
+__device__ __forceinline__ bool injected_stall(uint64_t *never, uint32_t stall_us,
+                                               volatile int *abort, int *status) {
+  if (stall_us == 0u) return true;
+  return mbar_wait_for(never, 0u, abort, status, kStatusTimeoutMma,
+                       static_cast<uint64_t>(stall_us) * 1000ull);
 }
 
 // Bounded wait that ignores the abort flag: on the way out of an aborted CTA

@@ -73,6 +73,19 @@ int map_err(cudaError_t e) {
   return NPL_ERR_INTERNAL;
 }
 
+// Fault injection (nplk_debug_fail_next_allocations): allocations still to
+// fail as out of memory.
+std::atomic<int> g_fail_allocs{0};
+
+// cudaMallocAsync, or an injected out-of-memory failure.
+cudaError_t device_alloc(void **p, size_t bytes, cudaStream_t s) {
+  int n = g_fail_allocs.load(std::memory_order_relaxed);
+  while (n > 0) {
+    if (g_fail_allocs.compare_exchange_weak(n, n - 1)) return cudaErrorMemoryAllocation;
+  }
+  return cudaMallocAsync(p, bytes, s);
+}
+
 // Kept for the thread's lifetime (no destructor: CUDA may already be shut
 // down when thread-local objects die at process exit).
 struct ThreadLanes {
@@ -210,7 +223,7 @@ void *Call::resolve(const void *p, size_t bytes, bool copy_in, bool copy_back) {
     }
   } else {
     // Plain or pinned host memory: stage through the device pool.
-    e = cudaMallocAsync(&b.dev, bytes, stream_);
+    e = device_alloc(&b.dev, bytes, stream_);
     if (e != cudaSuccess) {
       fail(map_err(e));
       return nullptr;
@@ -251,7 +264,7 @@ float *Call::param_out(float *p, size_t count) {
 void *Call::scratch(size_t bytes) {
   if (status_) return nullptr;
   void *d = nullptr;
-  cudaError_t e = cudaMallocAsync(&d, bytes < 256 ? 256 : bytes, stream_);
+  cudaError_t e = device_alloc(&d, bytes < 256 ? 256 : bytes, stream_);
   if (e != cudaSuccess) {
     fail(map_err(e));
     return nullptr;
@@ -263,7 +276,7 @@ void *Call::scratch(size_t bytes) {
 void *Call::try_scratch(size_t bytes) {
   if (status_) return nullptr;
   void *d = nullptr;
-  if (cudaMallocAsync(&d, bytes < 256 ? 256 : bytes, stream_) != cudaSuccess) {
+  if (device_alloc(&d, bytes < 256 ? 256 : bytes, stream_) != cudaSuccess) {
     cudaGetLastError();  // an allocation failure is not sticky; clear it
     return nullptr;
   }
@@ -335,3 +348,7 @@ int Call::finish(npl_perf_stats_t *stats, double flops, double bytes, const char
 }
 
 }  // namespace npl
+
+extern "C" int nplk_debug_fail_next_allocations(int count) {
+  return npl::g_fail_allocs.exchange(count > 0 ? count : 0);
+}

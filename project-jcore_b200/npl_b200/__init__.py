@@ -38,6 +38,8 @@ NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER = 3, 4
 NPLK_GEMM_TF32_FAST = 1
 NPLK_GEMM_SPLIT_OPERANDS = 2
 NPLK_GEMM_RAW_OPERANDS = 4
+NPLK_DEBUG_GEMM, NPLK_DEBUG_CONV_WINDOW = 1, 2
+NPLK_STATUS_TIMEOUT_MMA = 102
 
 
 class NplConfig(C.Structure):
@@ -197,6 +199,8 @@ NPLK_SIGNATURES = {
                                       C.c_uint, _VP, C.c_size_t, _VP]),
     "nplk_read_status": (C.c_int, [_VP]),
     "nplk_take_launch_count": (C.c_uint64, []),
+    "nplk_debug_arm_wait_timeout": (C.c_int, [C.c_int, C.c_uint32]),
+    "nplk_debug_fail_next_allocations": (C.c_int, [C.c_int]),
 }
 
 

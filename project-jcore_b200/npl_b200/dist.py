@@ -172,13 +172,28 @@ class PeerBuffers:
 
 
 def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=None,
-                              act: int = 0):
+                              act: int = 0, barrier_before: bool = False):
     """C = act(A @ B + bias) with B column-sharded, written by every rank
     straight into every rank's C (``peers.tensor``, row-major [M][N]) by the
-    GEMM epilogue (nplk_gemm_allgather). Asynchronous on the current stream:
-    C is complete on all ranks once every rank's stream has passed this call
-    (synchronise, then barrier)."""
+    GEMM epilogue (nplk_gemm_allgather). Asynchronous on the current stream.
+
+    Two orderings are the caller's to keep, because peers store straight into
+    this rank's C:
+      * after: C is complete on all ranks once every rank's stream has passed
+        this call (synchronise, then barrier);
+      * before: every rank must be done reading or writing its C from the
+        previous call before ANY rank issues the next one, or a fast rank's
+        stores overwrite a result a slower peer is still reading. Either
+        barrier before each call (``barrier_before=True`` synchronises this
+        rank's device and then barriers the process group), or order the
+        calls by a barrier the caller already has (one per iteration after
+        the completion barrier above suffices)."""
     import torch
+    import torch.distributed as dist
+
+    if barrier_before:
+        torch.cuda.synchronize(A.device)
+        dist.barrier(group=peers.group)
 
     lib = peers.lib
     M, K = A.shape

@@ -4,8 +4,9 @@ NPL code. The reference sources are compiled for the CPU by
 
 Every fixture is a small seeded case (inputs, parameters and the reference's
 outputs) saved as ``<name>.npz``. The tests use them to pin the C oracle
-(tests/test_oracle_golden.py) and the B200 library (tests/test_gpu_golden.py)
-to the reference on machines where the reference tree is absent.
+(tests/test_oracle_golden.py) and the B200 library (the golden cases of
+tests/test_gpu_gemm.py, test_gpu_conv.py and test_gpu_bandwidth.py) to the
+reference on machines where the reference tree is absent.
 
 Run:  python tests/golden/make_golden.py
 """

@@ -163,3 +163,19 @@ def test_multi_gpu_entry_points_argument_checks(lib):
     assert allgather(two, 2, -4, 128) == nb.NPL_ERR_INVALID_ARG          # negative column
     assert allgather(two, 2, 96, 128) == nb.NPL_ERR_INVALID_ARG          # block past ldc
     assert allgather(with_null, 2, 0, 128) == nb.NPL_ERR_INVALID_ARG     # a null destination
+
+
+def test_fault_injection_hooks_arm_and_disarm(lib):
+    # Arming touches no device: unknown kernel families and limits above a
+    # minute are rejected; 0 disarms. The allocation hook returns the count
+    # that was still armed.
+    assert lib.nplk_debug_arm_wait_timeout(0, 1000) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_debug_arm_wait_timeout(3, 1000) == nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_debug_arm_wait_timeout(nb.NPLK_DEBUG_GEMM, 60_000_001) == \
+        nb.NPL_ERR_INVALID_ARG
+    for which in (nb.NPLK_DEBUG_GEMM, nb.NPLK_DEBUG_CONV_WINDOW):
+        assert lib.nplk_debug_arm_wait_timeout(which, 1000) == 0
+        assert lib.nplk_debug_arm_wait_timeout(which, 0) == 0
+    assert lib.nplk_debug_fail_next_allocations(2) == 0
+    assert lib.nplk_debug_fail_next_allocations(-5) == 2
+    assert lib.nplk_debug_fail_next_allocations(0) == 0
