@@ -103,7 +103,8 @@ enum {
   NPLK_CONV_ALGO_DIRECT = 1,
   NPLK_CONV_ALGO_IM2COL = 2,
   NPLK_CONV_ALGO_WINDOW = 3,
-  NPLK_CONV_ALGO_WINDOW_GATHER = 4
+  NPLK_CONV_ALGO_WINDOW_GATHER = 4,
+  NPLK_CONV_ALGO_WINDOW_PAIR = 5 /* the gather windows on CTA pairs (M = 256 MMAs over two SMs) */
 };
 
 /* Workspace bytes of nplk_conv2d_run_algo with `algo`; 0 when the geometry
@@ -301,6 +302,67 @@ NPL_API int nplk_read_status(void *stream);
 /* Number of library kernels launched on this thread since the last call
  * (resets the counter). */
 NPL_API uint64_t nplk_take_launch_count(void);
+
+/* ---- tile-configuration cache ---------------------------------------------- */
+/* Replaces the reference's tuning result cache (composite/tuning_rCache/src/
+ * tuning_cache.cpp:186-506; cat_* API in include/cached_autotuner.h): the
+ * kernel choice measured fastest per (operation, shape, SM count), consulted
+ * by the AUTO paths of nplk_conv2d_run / nplk_conv2d_fused (the conv kernel,
+ * NPLK_CONV_ALGO_*) and nplk_gemm (the output-tile width BN, 64 or 128), and
+ * persisted as a text file with a format version and a hardware signature
+ * (device name, compute capability, SM count, L2 size) checked on load.
+ * npl_init loads the file named by NPL_TUNING_CACHE (if set and present) and
+ * npl_shutdown writes it back; NPL_AUTOTUNE=1 makes npl_conv2d_bn_activation,
+ * npl_conv2d and npl_matmul tune a shape on its first call. Thread safe. */
+typedef struct {
+  uint64_t entries;   /* entries held */
+  uint64_t hits;      /* AUTO lookups that found an entry */
+  uint64_t misses;    /* AUTO lookups that did not */
+  uint64_t tunes;     /* entries written by nplk_*_tune */
+  uint64_t evictions; /* entries dropped by the entry limit */
+} nplk_tuning_stats_t;
+
+/* Merges a cache file into the cache; returns the entries read, or
+ * NPL_ERR_INVALID_ARG (unreadable or malformed file) or NPL_ERR_UNSUPPORTED
+ * (another format version or another device: nothing is loaded). */
+NPL_API int nplk_tuning_cache_load(const char *path);
+/* Writes the cache (atomically, through a temporary file); returns the
+ * entries written or NPL_ERR_INTERNAL on an I/O error. */
+NPL_API int nplk_tuning_cache_save(const char *path);
+/* Drops every entry and zeroes the statistics. */
+NPL_API void nplk_tuning_cache_clear(void);
+NPL_API int nplk_tuning_cache_stats(nplk_tuning_stats_t *out);
+/* Keeps at most n entries, evicting the oldest inserted (0 = unlimited). */
+NPL_API int nplk_tuning_cache_set_max_entries(size_t n);
+/* The cache key of a conv geometry or a GEMM shape on the current device,
+ * written NUL-terminated into buf (truncated to len); returns its length. */
+NPL_API size_t nplk_tuning_key_conv(const nplk_conv_geom_t *g, char *buf, size_t len);
+NPL_API size_t nplk_tuning_key_gemm(int64_t M, int64_t N, int64_t K, char *buf, size_t len);
+/* Direct access to entries (import / export tooling, tests): put inserts or
+ * replaces; get returns 1 and fills choice / us when present, else 0. */
+NPL_API int nplk_tuning_cache_put(const char *key, int choice, float us);
+NPL_API int nplk_tuning_cache_get(const char *key, int *choice, float *us);
+
+/* Measures every conv kernel the geometry and the workspace allow (size the
+ * workspace with the largest nplk_conv_workspace_size_algo to try them all)
+ * on the caller's tensors: `reps` timed runs each after one warm-up, median
+ * device time. Caches the fastest, returns it in *best_algo (and its median
+ * time in *best_us when non-NULL) and leaves the conv's output in `out` (all
+ * kernels give the same bits). Synchronises `stream`. Arguments as
+ * nplk_conv2d_fused. */
+NPL_API int nplk_conv2d_tune(void *stream, const nplk_conv_geom_t *g, const float *x,
+                             const float *w, const float *bias, const float *bn_mean,
+                             const float *bn_var, const float *bn_gamma, const float *bn_beta,
+                             float bn_eps, int act, float act_alpha, float *out,
+                             void *workspace, size_t workspace_bytes, int reps, int *best_algo,
+                             float *best_us);
+/* The same for the GEMM's tile width: C = A @ B (alpha 1, beta 0) with BN 64
+ * and 128, `reps` timed runs each; caches and returns the faster BN. The
+ * workspace is the split form's (nplk_gemm_workspace_size). */
+NPL_API int nplk_gemm_tune(void *stream, int64_t M, int64_t N, int64_t K, const float *A,
+                           int64_t lda, const float *B, int64_t ldb, float *C, int64_t ldc,
+                           void *workspace, size_t workspace_bytes, int reps, int *best_bn,
+                           float *best_us);
 
 /* ---- fault injection (tests of the failure paths) --------------------------- */
 /* No reference counterpart: the reference's CPU loops cannot time out or run

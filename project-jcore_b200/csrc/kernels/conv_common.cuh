@@ -84,13 +84,20 @@ __device__ __forceinline__ void conv_store_chunk(float *__restrict__ y, int64_t 
 // across them); `acc_tmem` is the accumulator's first column. The tile's
 // constants are staged in shared memory (every lane reads the same channel,
 // so each read is a broadcast). Returns false when the CTA aborted.
-template <int BNC, int kAct>
+// kPair: the accumulator belongs to a CTA pair (conv_window_pair.cu); the
+// wait acquires at cluster scope and a timeout also raises the peer's abort
+// flag (`peer_abort`, its shared::cluster address).
+template <int BNC, int kAct, bool kPair = false>
 __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t acc_tmem,
                                                    int quad, int lane, int et, int mb, int nb,
                                                    float4 *ep_s, float *ep_beta_s,
                                                    uint64_t *acc_full, uint32_t acc_phase,
-                                                   volatile int *abort_flag) {
-  mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
+                                                   volatile int *abort_flag,
+                                                   uint32_t peer_abort = 0u) {
+  if constexpr (kPair)
+    mbar_wait_pair(acc_full, acc_phase, abort_flag, peer_abort, p.status, kStatusTimeoutEpilogue);
+  else
+    mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
   // All four warps pass this barrier before anyone rewrites the constants of
   // the previous tile, and they leave together if the CTA aborted.
   named_barrier_sync(1, 128);
@@ -161,6 +168,14 @@ int launch_nchw_to_nhwc_split(cudaStream_t s, const float *x, float *hi, float *
 int launch_conv_window(cudaStream_t s, int bnc, const float *wsplit, int64_t kp, int64_t n_blocks,
                        const float *x_nhwc, ConvParams prm, int n_img, bool after_prep = false);
 bool conv_window_supported(const ConvParams &prm, int n_img);
+
+// Window-gather conv on CTA pairs (conv_window_pair.cu): every MMA spans two
+// SMs (tcgen05 cta_group::2), each SM reading half of the weight operand.
+// Needs the gather form's conditions, C_out <= 64 (one output-channel block
+// of 64) and taps shared along the row (stride_w 1, KW > 1, (KW-1)*dw <= 8).
+bool conv_window_pair_supported(const ConvParams &prm, int n_img, int bnc, int64_t n_blocks);
+int launch_conv_window_pair(cudaStream_t s, const float *wsplit, int64_t kp, ConvParams prm,
+                            int n_img, bool after_prep);
 // The gather variant also needs x to have fewer than 2^31 elements.
 bool conv_window_gather_supported(const ConvParams &prm, int n_img);
 void conv_window_rows(const ConvParams &p, int *wv, int64_t *mv);

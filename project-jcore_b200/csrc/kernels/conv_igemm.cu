@@ -36,10 +36,13 @@
 // split, zero-pad) together with the per-channel epilogue constants.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <vector>
 
 #include "conv_common.cuh"
 #include "nplk_host.h"
+#include "tuning_cache.h"
 
 namespace nplk {
 
@@ -433,6 +436,7 @@ enum ConvPath {
   kPathIm2col = 1,  // NHWC hi/lo planes + im2col TMA per k-block (conv_im2col.cu)
   kPathWindow = 2,  // raw NHWC plane + im2col TMA windows shared by the KW taps (conv_window.cu)
   kPathWindowGather = 3,  // the same windows gathered from NCHW x by the kernel itself
+  kPathWindowPair = 4,    // the gather windows on CTA pairs (conv_window_pair.cu)
 };
 
 // Workspace layout: [W' split: w_bytes][epilogue constants: ep_bytes], then
@@ -484,7 +488,8 @@ ConvParams conv_params(const nplk_conv_geom_t *g, const ConvPlan &c) {
 // does not suit it. AUTO picks the shared-window gather kernel for stride-1
 // filters wider than one column, the per-k-block im2col kernel for the
 // other TMA-eligible geometries and the direct kernel otherwise.
-ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
+ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO,
+                   bool use_cache = true) {
   ConvPlan c{};
   c.bnc = g->c_out <= 64 ? 64 : 128;
   const int slots = conv_row_slots(g->c_in, g->kw, g->dil_w);
@@ -501,6 +506,7 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
   const bool window_ok = conv_window_supported(prm, n);
   const bool gather_ok = conv_window_gather_supported(prm, n);
   const bool im2col_ok = conv_im2col_supported(prm, n);
+  const bool pair_ok = conv_window_pair_supported(prm, n, c.bnc, c.n_blocks);
   const bool shared_taps = g->stride_w == 1 && g->kw > 1;
   switch (algo) {
     case NPLK_CONV_ALGO_AUTO:
@@ -521,10 +527,21 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO) {
     case NPLK_CONV_ALGO_WINDOW_GATHER:
       c.path = gather_ok ? kPathWindowGather : -1;
       break;
+    case NPLK_CONV_ALGO_WINDOW_PAIR:
+      c.path = pair_ok ? kPathWindowPair : -1;
+      break;
     default:
       c.path = -1;
   }
   c.planes = c.path == kPathIm2col ? 2 : c.path == kPathWindow ? 1 : 0;
+  // AUTO takes the kernel the tile-configuration cache measured fastest for
+  // this geometry on this device (nplk_conv2d_tune), when there is one.
+  int cached = 0;
+  if (algo == NPLK_CONV_ALGO_AUTO && use_cache && !tuning_cache_empty() &&
+      tuning_lookup(tuning_key_conv(g), &cached) && cached != NPLK_CONV_ALGO_AUTO) {
+    const ConvPlan t = plan_conv(g, cached, false);
+    if (t.path >= 0) return t;
+  }
   return c;
 }
 
@@ -696,6 +713,9 @@ int run_plan(cudaStream_t s, const nplk_conv_geom_t *g, const float *x, const Co
     case kPathWindowGather:
       prm.x = x;
       return launch_conv_window(s, c.bnc, wsplit, c.kp, c.n_blocks, nullptr, prm, n, after_prep);
+    case kPathWindowPair:
+      prm.x = x;
+      return launch_conv_window_pair(s, wsplit, c.kp, prm, n, after_prep);
     case kPathWindow:
     case kPathIm2col: {
       if (stage) {
@@ -753,8 +773,15 @@ int run_auto(void *stream, const nplk_conv_geom_t *g, const float *x, int act, f
   if (rc) return rc;
   if (!x) return kErrInvalidArg;
   // A workspace too small for the planes of the chosen kernel selects the
-  // direct kernel (same results).
-  if (workspace_bytes < c.full_bytes()) c.path = kPathDirect;
+  // kernel AUTO picks without the tile-configuration cache if that fits, else
+  // the direct kernel (same results either way).
+  if (workspace_bytes < c.full_bytes()) {
+    const ConvPlan h = plan_conv(g, NPLK_CONV_ALGO_AUTO, false);
+    if (workspace_bytes >= h.full_bytes())
+      c = h;
+    else
+      c.path = kPathDirect;
+  }
   return run_plan(static_cast<cudaStream_t>(stream), g, x, c, prm, workspace, true, after_prep);
 }
 
@@ -792,3 +819,62 @@ extern "C" int nplk_conv2d_fused(void *stream, const nplk_conv_geom_t *g, const 
   if (rc) return rc;
   return run_auto(stream, g, x, act, act_alpha, out, workspace, workspace_bytes, status, true);
 }
+
+extern "C" int nplk_conv2d_tune(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                const float *w, const float *bias, const float *bn_mean,
+                                const float *bn_var, const float *bn_gamma,
+                                const float *bn_beta, float bn_eps, int act, float act_alpha,
+                                float *out, void *workspace, size_t workspace_bytes, int reps,
+                                int *best_algo, float *best_us) {
+  if (!x || !w || !out || !best_algo || reps < 1 || reps > 1000) return kErrInvalidArg;
+  int rc = nplk_conv2d_prepare(stream, g, w, bias, bn_mean, bn_var, bn_gamma, bn_beta, bn_eps,
+                               workspace, workspace_bytes);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+    if (e0) cudaEventDestroy(e0);
+    return kErrInternal;
+  }
+  int best = 0;
+  float best_ms = 0.0f;
+  for (int algo : {NPLK_CONV_ALGO_DIRECT, NPLK_CONV_ALGO_IM2COL, NPLK_CONV_ALGO_WINDOW,
+                   NPLK_CONV_ALGO_WINDOW_GATHER, NPLK_CONV_ALGO_WINDOW_PAIR}) {
+    const ConvPlan c = plan_conv(g, algo, false);
+    if (c.path < 0 || workspace_bytes < c.full_bytes()) continue;  // not a candidate here
+    std::vector<float> ms;
+    for (int r = 0; r <= reps && rc == kOk; ++r) {
+      if (cudaEventRecord(e0, s) != cudaSuccess) rc = kErrInternal;
+      if (rc == kOk)
+        rc = nplk_conv2d_run_algo(stream, g, x, act, act_alpha, out, workspace, workspace_bytes,
+                                  nullptr, algo);
+      if (rc == kOk && (cudaEventRecord(e1, s) != cudaSuccess ||
+                        cudaEventSynchronize(e1) != cudaSuccess))
+        rc = kErrInternal;
+      float t = 0.0f;
+      if (rc == kOk && r > 0) {  // the first run is the warm-up
+        cudaEventElapsedTime(&t, e0, e1);
+        ms.push_back(t);
+      }
+    }
+    if (rc != kOk) break;
+    std::nth_element(ms.begin(), ms.begin() + ms.size() / 2, ms.end());
+    const float med = ms[ms.size() / 2];
+    if (best == 0 || med < best_ms) {
+      best = algo;
+      best_ms = med;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc != kOk) return rc;
+  if (best == 0) return kErrUnsupported;
+  if (nplk_read_status(stream) != 0) return kErrInternal;
+  // The last candidate run left its output in `out`; every kernel writes
+  // the same bits, so it is the conv's result.
+  tuning_insert(tuning_key_conv(g), best, best_ms * 1000.0);
+  *best_algo = best;
+  if (best_us) *best_us = best_ms * 1000.0f;
+  return kOk;
+}
+

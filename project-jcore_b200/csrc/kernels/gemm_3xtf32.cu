@@ -21,9 +21,13 @@
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "nplk_device.cuh"
 #include "nplk_host.h"
 #include "ptx_sm100.cuh"
+#include "tuning_cache.h"
 
 namespace nplk {
 
@@ -619,17 +623,27 @@ struct GemmPlan {
   int bn;
   int64_t m_blocks, n_blocks, kp;
   size_t a_bytes, b_bytes;
+  size_t b_bytes_max;  // B' for either tile width (the workspace size covers both)
 };
 
-GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K) {
+// Output-tile width: force_bn when 64 or 128, else the tile-configuration
+// cache's entry for the shape, else 128 when the 128-wide tiles fill the SMs.
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int force_bn = 0) {
   GemmPlan g{};
   g.m_blocks = ceil_div(M, kGemmBM);
   g.kp = ceil_div(K, kGemmBK) * kGemmBK;
   const int64_t tiles128 = g.m_blocks * ceil_div(N, 128);
   g.bn = (tiles128 >= sm_count()) ? 128 : 64;
+  int cached = 0;
+  if (force_bn == 64 || force_bn == 128)
+    g.bn = force_bn;
+  else if (!tuning_cache_empty() && tuning_lookup(tuning_key_gemm(M, N, K), &cached) &&
+           (cached == 64 || cached == 128))
+    g.bn = cached;
   g.n_blocks = ceil_div(N, g.bn);
   g.a_bytes = align_up(static_cast<size_t>(g.m_blocks) * 2 * kGemmBM * g.kp * 4, 256);
   g.b_bytes = align_up(static_cast<size_t>(g.n_blocks) * 2 * g.bn * g.kp * 4, 256);
+  g.b_bytes_max = align_up(static_cast<size_t>(ceil_div(N, 128)) * 2 * 128 * g.kp * 4, 256);
   return g;
 }
 
@@ -717,7 +731,7 @@ using namespace nplk;
 extern "C" size_t nplk_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   const GemmPlan g = plan_gemm(M, N, K);
-  return g.a_bytes + g.b_bytes;
+  return g.a_bytes + g.b_bytes_max;
 }
 
 namespace nplk {
@@ -728,12 +742,12 @@ namespace {
 // select; `pd` non-null selects the fused exchange epilogue.
 int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, int64_t lda,
              const float *B, int64_t ldb, GemmParams prm, const GemmDst *pd, unsigned flags,
-             void *workspace, size_t workspace_bytes, int *status) {
+             void *workspace, size_t workspace_bytes, int *status, int force_bn = 0) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return kErrInvalidArg;
   if (lda < K || ldb < N) return kErrInvalidArg;
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
     return kErrUnsupported;
-  const GemmPlan g = plan_gemm(M, N, K);
+  const GemmPlan g = plan_gemm(M, N, K, force_bn);
   if (!status) status = device_status_word();
   if (!status) return kErrInternal;
   prm.M = static_cast<int>(M);
@@ -828,3 +842,57 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
   return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, &pd,
                   flags, workspace, workspace_bytes, status);
 }
+
+extern "C" int nplk_gemm_tune(void *stream, int64_t M, int64_t N, int64_t K, const float *A,
+                              int64_t lda, const float *B, int64_t ldb, float *C, int64_t ldc,
+                              void *workspace, size_t workspace_bytes, int reps, int *best_bn,
+                              float *best_us) {
+  if (!C || ldc < N || !best_bn || reps < 1 || reps > 1000) return kErrInvalidArg;
+  if (M <= 0 || N <= 0 || K <= 0) return kErrInvalidArg;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  GemmParams prm{};
+  prm.alpha = 1.0f;
+  prm.beta = 0.0f;
+  prm.C = C;
+  prm.ldc = ldc;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+    if (e0) cudaEventDestroy(e0);
+    return kErrInternal;
+  }
+  int best = 0, rc = kOk;
+  float best_ms = 0.0f;
+  for (int bn : {64, 128}) {
+    std::vector<float> ms;
+    for (int r = 0; r <= reps && rc == kOk; ++r) {
+      if (cudaEventRecord(e0, s) != cudaSuccess) rc = kErrInternal;
+      if (rc == kOk)
+        rc = gemm_run(s, M, N, K, A, lda, B, ldb, prm, nullptr, 0u, workspace, workspace_bytes,
+                      nullptr, bn);
+      if (rc == kOk && (cudaEventRecord(e1, s) != cudaSuccess ||
+                        cudaEventSynchronize(e1) != cudaSuccess))
+        rc = kErrInternal;
+      float t = 0.0f;
+      if (rc == kOk && r > 0) {  // the first run is the warm-up
+        cudaEventElapsedTime(&t, e0, e1);
+        ms.push_back(t);
+      }
+    }
+    if (rc != kOk) break;
+    std::nth_element(ms.begin(), ms.begin() + ms.size() / 2, ms.end());
+    const float med = ms[ms.size() / 2];
+    if (best == 0 || med < best_ms) {
+      best = bn;
+      best_ms = med;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc != kOk) return rc;
+  if (nplk_read_status(stream) != 0) return kErrInternal;
+  tuning_insert(tuning_key_gemm(M, N, K), best, best_ms * 1000.0);
+  *best_bn = best;
+  if (best_us) *best_us = best_ms * 1000.0f;
+  return kOk;
+}
+

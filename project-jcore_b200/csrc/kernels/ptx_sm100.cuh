@@ -356,6 +356,135 @@ __device__ __forceinline__ void tmem_wait_ld2(uint32_t (&r)[32], uint32_t (&s)[3
 }
 
 // ---------------------------------------------------------------------------
+// CTA pairs (cluster of two CTAs on neighbouring SMs, tcgen05 cta_group::2).
+// The pair's leader (cluster rank 0) issues the MMAs; each MMA reads A rows
+// and half of B from each CTA's shared memory at the same offsets and writes
+// each CTA's own TMEM. No multicast loads: each CTA loads its own operands.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address in the shared::cluster window of the variable at local shared
+// address `local` in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+// Arrives once on an mbarrier given by its shared::cluster address (this
+// CTA's or the peer's), releasing this thread's prior writes at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return done;
+}
+
+// mbar_wait with acquire at cluster scope (the barrier also receives arrivals
+// from the peer CTA or the pair's MMA commits). On failure the local abort
+// flag is raised and so is the peer's (`peer_abort`: its shared::cluster
+// address), so both CTAs of the pair leave their loops.
+__device__ __forceinline__ bool mbar_wait_pair(uint64_t *bar, uint32_t parity,
+                                               volatile int *abort, uint32_t peer_abort,
+                                               int *status, int code) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 31u) == 0u) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
+        atomicCAS(status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// Raises the peer CTA's abort flag (shared::cluster address).
+__device__ __forceinline__ void pair_raise_abort(uint32_t peer_abort) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1) : "memory");
+}
+
+// Cluster-wide barrier of all threads of both CTAs (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+
+// TMEM allocation for a CTA pair: the same warp of both CTAs executes it and
+// both receive the same base address.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// D (+)= A * B^T for the pair, kind::tf32, M = 256 (128 rows of A from each
+// CTA), N given by idesc (N/2 rows of B from each CTA). Issued by one thread
+// of the leader.
+__device__ __forceinline__ void mma_tf32_ss_pair(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// When the pair MMAs issued so far by this thread complete, arrives once on
+// the mbarrier at the same shared-memory offset as `bar` in both CTAs of the
+// pair (CTA mask 0b11). This is the completion signal of tcgen05, not a data
+// copy: nothing is loaded or stored.
+__device__ __forceinline__ void mma_commit_pair_both(uint64_t *bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// 2-D tile load into this CTA's shared memory whose completion (transaction
+// bytes) is signalled on the pair leader's mbarrier `leader_bar` (a
+// shared::cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap *map, uint32_t leader_bar,
+                                                 void *dst, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // UMMA descriptors
 // ---------------------------------------------------------------------------
 // Shared-memory matrix descriptor for a K-major operand stored in the

@@ -2,6 +2,7 @@
 // (reference: advanced/neural_layer/src/npl_convolution.cpp:13-246, 904-991).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 
 #include "npl_runtime.h"
@@ -227,13 +228,27 @@ int run_conv(const npl_tensor_t *input, const npl_tensor_t *weights, const npl_t
     gamma = call.param(bn->gamma, co);
     beta = call.param(bn->beta, co);
   }
-  const size_t ws = nplk_conv_workspace_size(&g);
+  // NPL_AUTOTUNE=1: a geometry without a tile-configuration cache entry is
+  // tuned on this call (every conv kernel timed, the fastest cached), which
+  // needs the workspace of the largest candidate.
+  const bool tune = npl::autotune_mode() && !npl::conv_tuned(&g);
+  size_t ws = nplk_conv_workspace_size(&g);
+  if (tune)
+    for (int a = NPLK_CONV_ALGO_DIRECT; a <= NPLK_CONV_ALGO_WINDOW_PAIR; ++a)
+      ws = std::max(ws, nplk_conv_workspace_size_algo(&g, a));
   void *work = call.scratch(ws);
   if (call.status()) return call.finish(nullptr, 0, 0, nullptr);
   call.start_timer();
-  call.fail(nplk_conv2d_fused(call.stream(), &g, x, w, b, mean, var, gamma, beta,
-                              bn ? bn->epsilon : 0.0f, train_bn ? NPLK_ACT_NONE : act,
-                              act_alpha, y, work, ws, nullptr));
+  const float eps = bn ? bn->epsilon : 0.0f;
+  const int conv_act = train_bn ? NPLK_ACT_NONE : act;
+  if (tune) {
+    int algo = 0;
+    call.fail(nplk_conv2d_tune(call.stream(), &g, x, w, b, mean, var, gamma, beta, eps, conv_act,
+                               act_alpha, y, work, ws, 3, &algo, nullptr));
+  } else {
+    call.fail(nplk_conv2d_fused(call.stream(), &g, x, w, b, mean, var, gamma, beta, eps,
+                                conv_act, act_alpha, y, work, ws, nullptr));
+  }
   int fused = 1 + (bn ? 1 : 0) + (act != NPLK_ACT_NONE ? 1 : 0);
   if (train_bn && !call.status()) {
     // Training-mode BN needs batch statistics of the conv output, so it runs

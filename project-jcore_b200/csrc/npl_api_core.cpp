@@ -4,6 +4,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "npl_runtime.h"
@@ -92,6 +93,17 @@ extern "C" int npl_init(const npl_config_t *config) {
   s.total_ops = 0;
   s.total_fused = 0;
   s.initialized = true;
+  // The tile-configuration cache file, if one is named and present (a file
+  // from another device or format version is reported and skipped).
+  const char *cache_path = std::getenv("NPL_TUNING_CACHE");
+  if (cache_path && cache_path[0]) {
+    if (FILE *f = std::fopen(cache_path, "r")) {
+      std::fclose(f);
+      const int n = nplk_tuning_cache_load(cache_path);
+      if (s.config.verbose && n >= 0)
+        std::printf("[NPL] Loaded %d tuning entries from %s\n", n, cache_path);
+    }
+  }
   if (s.config.verbose) {
     std::printf("[NPL] Initialized on device %d (%s, %d SMs)\n", dev, prop.name,
                 prop.multiProcessorCount);
@@ -109,6 +121,10 @@ extern "C" void npl_shutdown(void) {
   }
   cudaSetDevice(s.device);
   cudaStreamSynchronize(s.stream);
+  const char *cache_path = std::getenv("NPL_TUNING_CACHE");
+  nplk_tuning_stats_t ts{};
+  if (cache_path && cache_path[0] && nplk_tuning_cache_stats(&ts) == 0 && ts.entries > 0)
+    nplk_tuning_cache_save(cache_path);
   cudaStreamDestroy(s.stream);
   s.stream = nullptr;
   s.initialized = false;

@@ -148,6 +148,14 @@ extern "C" int npl_matmul(const npl_tensor_t *A, const npl_tensor_t *B, npl_tens
   if (call.status()) return call.finish(nullptr, 0, 0, nullptr);
   const unsigned flags = npl::tf32_fast_mode() ? NPLK_GEMM_TF32_FAST : 0u;
   call.start_timer();
+  // NPL_AUTOTUNE=1: an untuned shape has its tile width measured once (into
+  // C, which the call then overwrites) and cached; beta == 0 only, since the
+  // measurement does not keep C.
+  if (w && batch == 1 && beta == 0.0f && flags == 0u && npl::autotune_mode() &&
+      !npl::gemm_tuned(M, N, K)) {
+    int bn = 0;
+    call.fail(nplk_gemm_tune(call.stream(), M, N, K, a, K, b, N, c, N, w, ws, 3, &bn, nullptr));
+  }
   for (size_t i = 0; i < batch && !call.status(); ++i) {
     const int rc = nplk_gemm(call.stream(), M, N, K, alpha, a + i * M * K, K,
                              b + (b_batched ? i * K * N : 0), N, beta, c + i * M * N, N,

@@ -49,6 +49,23 @@ bool tf32_fast_mode() {
   return e && e[0] == '1';
 }
 
+bool autotune_mode() {
+  const char *e = std::getenv("NPL_AUTOTUNE");
+  return e && e[0] == '1';
+}
+
+bool conv_tuned(const nplk_conv_geom_t *g) {
+  char key[256];
+  nplk_tuning_key_conv(g, key, sizeof(key));
+  return nplk_tuning_cache_get(key, nullptr, nullptr) == 1;
+}
+
+bool gemm_tuned(int64_t M, int64_t N, int64_t K) {
+  char key[256];
+  nplk_tuning_key_gemm(M, N, K, key, sizeof(key));
+  return nplk_tuning_cache_get(key, nullptr, nullptr) == 1;
+}
+
 int validate_conv_params(const npl_conv_params_t *p) {
   // ValidateConvParams, npl_convolution.cpp:1347-1365.
   if (!p) return NPL_ERR_INVALID_ARG;

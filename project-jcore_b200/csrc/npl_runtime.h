@@ -39,6 +39,14 @@ int validate_tensor(const npl_tensor_t *t, const char *name);
 // True when NPL_TF32_FAST=1 selects one-pass TF32 for the dense contractions.
 bool tf32_fast_mode();
 
+// True when NPL_AUTOTUNE=1: npl_* calls tune a shape that has no entry in the
+// tile-configuration cache (nplk_conv2d_tune / nplk_gemm_tune) on its first
+// call.
+bool autotune_mode();
+// Whether the cache holds an entry for the conv geometry / GEMM shape.
+bool conv_tuned(const nplk_conv_geom_t *g);
+bool gemm_tuned(int64_t M, int64_t N, int64_t K);
+
 // One API call: resolves tensor pointers to device memory on the library's
 // device, stages plain host memory through the stream-ordered pool, times the
 // launched kernels with CUDA events, copies staged outputs back, synchronises

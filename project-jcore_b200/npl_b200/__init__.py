@@ -34,7 +34,7 @@ NPL_PAD_VALID, NPL_PAD_SAME, NPL_PAD_EXPLICIT = 0, 1, 2
 NPL_POOL_MAX, NPL_POOL_AVG, NPL_POOL_GLOBAL_AVG, NPL_POOL_GLOBAL_MAX = 0, 1, 2, 3
 NPL_MAX_DIMS = 8
 NPLK_CONV_ALGO_AUTO, NPLK_CONV_ALGO_DIRECT, NPLK_CONV_ALGO_IM2COL = 0, 1, 2
-NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER = 3, 4
+NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER, NPLK_CONV_ALGO_WINDOW_PAIR = 3, 4, 5
 NPLK_GEMM_TF32_FAST = 1
 NPLK_GEMM_SPLIT_OPERANDS = 2
 NPLK_GEMM_RAW_OPERANDS = 4
@@ -123,6 +123,10 @@ class NplkConvGeom(C.Structure):
         "pad_top", "pad_left", "dil_h", "dil_w", "h_out", "w_out")]
 
 
+class NplkTuningStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("entries", "hits", "misses", "tunes", "evictions")]
+
+
 _P = C.POINTER
 _T = _P(NplTensor)
 _S = _P(NplPerfStats)
@@ -199,6 +203,19 @@ NPLK_SIGNATURES = {
                                       C.c_uint, _VP, C.c_size_t, _VP]),
     "nplk_read_status": (C.c_int, [_VP]),
     "nplk_take_launch_count": (C.c_uint64, []),
+    "nplk_tuning_cache_load": (C.c_int, [C.c_char_p]),
+    "nplk_tuning_cache_save": (C.c_int, [C.c_char_p]),
+    "nplk_tuning_cache_clear": (None, []),
+    "nplk_tuning_cache_stats": (C.c_int, [_P(NplkTuningStats)]),
+    "nplk_tuning_cache_set_max_entries": (C.c_int, [C.c_size_t]),
+    "nplk_tuning_key_conv": (C.c_size_t, [_G, C.c_char_p, C.c_size_t]),
+    "nplk_tuning_key_gemm": (C.c_size_t, [_I64, _I64, _I64, C.c_char_p, C.c_size_t]),
+    "nplk_tuning_cache_put": (C.c_int, [C.c_char_p, C.c_int, _F]),
+    "nplk_tuning_cache_get": (C.c_int, [C.c_char_p, _P(C.c_int), _P(C.c_float)]),
+    "nplk_conv2d_tune": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F, C.c_int, _F,
+                                   _VP, _VP, C.c_size_t, C.c_int, _P(C.c_int), _P(C.c_float)]),
+    "nplk_gemm_tune": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _I64, _VP, _I64, _VP, _I64, _VP,
+                                 C.c_size_t, C.c_int, _P(C.c_int), _P(C.c_float)]),
     "nplk_debug_arm_wait_timeout": (C.c_int, [C.c_int, C.c_uint32]),
     "nplk_debug_fail_next_allocations": (C.c_int, [C.c_int]),
 }

@@ -3,7 +3,9 @@ and the oracle:
   * IM2COL: NHWC tf32 hi/lo planes of x, one im2col TMA load per k-block;
   * WINDOW: one raw NHWC plane, one im2col TMA window per (tile, channel
     block, kh) shared by the KW taps (tf32 lo part formed in shared memory);
-  * WINDOW_GATHER: the same windows gathered from NCHW x by the kernel.
+  * WINDOW_GATHER: the same windows gathered from NCHW x by the kernel;
+  * WINDOW_PAIR: the gather windows on CTA pairs, each MMA spanning two SMs
+    (C_out <= 64).
 
 All kernels share the k order, the split, the MMA sequence and the
 epilogue, so their outputs must agree bit for bit; the launch counter shows
@@ -66,7 +68,8 @@ CASES = {
 
 
 ALGOS = {nb.NPLK_CONV_ALGO_DIRECT: 1, nb.NPLK_CONV_ALGO_IM2COL: 2, nb.NPLK_CONV_ALGO_WINDOW: 2,
-         nb.NPLK_CONV_ALGO_WINDOW_GATHER: 1}  # algo -> kernel launches per run
+         nb.NPLK_CONV_ALGO_WINDOW_GATHER: 1,
+         nb.NPLK_CONV_ALGO_WINDOW_PAIR: 1}  # algo -> kernel launches per run
 
 
 def _run(lib, g, x, w, bias, bn, act, algo, ws_bytes, work):
