@@ -522,93 +522,121 @@ def run_b200(args, rank, world, local_rank):
 
 
 def bandwidth_also(lib, local_rank, reps=10):
-    """The bandwidth-bound primitives on one GPU, each on tensors larger than
-    L2 (N=256, C=512, 14x14 NCHW = 103 MB; LN on 8192 x 4096; softmax over
-    102400 rows of 1000):
-    median CUDA-event time of `reps` launches with L2 flushed before each,
-    algorithmic bytes (each input read once, each output written once) per
-    second and the fraction of the measured HBM copy bandwidth."""
+    """The bandwidth-bound primitives on one GPU at the workload's size
+    (N=256, C=512, 14x14 NCHW = 103 MB; layer norm on 8192 x 4096; softmax
+    over 102400 rows of 1000) and at four times that size: median CUDA-event
+    time of `reps` launches with L2 flushed before each, algorithmic bytes
+    (each input read once, each output written once) per second, and the
+    fraction of the measured HBM copy bandwidth.
+
+    At the workload's size an output of ~100 MB is still largely dirty in the
+    126 MB L2 when the end event fires, so write-heavy kernels read high
+    (an upper bound) and read-only ones low; the 4x figures (outputs well
+    beyond L2, ramp-up amortised) are the steady-state DRAM rates. Two
+    size-matched references are timed the same way: a device copy and a pure
+    read (a sum) of the same tensor."""
     import torch
     dev = torch.device("cuda", local_rank)
-    gen = torch.Generator(device=dev).manual_seed(0)
     s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
     p = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
-    n, c, hw = 256, 512, 14
-    x = torch.randn(n, c, hw, hw, device=dev, generator=gen)
-    y = torch.empty_like(x)
-    w = torch.randn(c, 1, 3, 3, device=dev, generator=gen) * 0.3
-    bn = [torch.rand(c, device=dev, generator=gen) + 0.5 for _ in range(4)]
-    gap = torch.empty(n * c, device=dev)
-    pooled = torch.empty(n, c, 7, 7, device=dev)
-    rows = torch.randn(8192, 4096, device=dev, generator=gen)
-    rows_y = torch.empty_like(rows)
-    logits = torch.randn(102400, 1000, device=dev, generator=gen)
-    probs = torch.empty_like(logits)
-    g = nb.conv_geom(n, c, hw, hw, c, 3, 3, 1, 1)
     flush = make_l2_flush(dev)
-    nx = x.numel()
-    cases = [
-        ("depthwise 3x3", nx * 8 + w.numel() * 4,
-         lambda: lib.nplk_depthwise_conv2d(s, C.byref(g), p(x), p(w), None, p(y))),
-        ("batch_norm inference", nx * 8,
-         lambda: lib.nplk_batch_norm_infer(s, n, c, hw * hw, p(x), p(y), p(bn[0]), p(bn[1]),
-                                           p(bn[2]), p(bn[3]), 1e-5)),
-        ("relu", nx * 8, lambda: lib.nplk_activation(s, nx, p(x), p(y), 1, 0.0, 0)),
-        ("max pool 3x3/s2", nx * 4 + pooled.numel() * 4,
-         lambda: lib.nplk_pool2d(s, n, c, hw, hw, 3, 3, 2, 2, 1, 1, 7, 7, 0, 0, p(x),
-                                 p(pooled))),
-        ("global avg pool", nx * 4 + gap.numel() * 4,
-         lambda: lib.nplk_global_avg_pool(s, n * c, hw * hw, p(x), p(gap))),
-        ("softmax rows of 1000", logits.numel() * 8,
-         lambda: lib.nplk_softmax(s, 102400, 1000, 1, p(logits), p(probs))),
-        ("layer_norm 8192x4096", rows.numel() * 8,
-         lambda: lib.nplk_layer_norm(s, 8192, 4096, p(rows), p(rows_y), None, None, 1e-5)),
-    ]
-    # The depthwise -> BN -> ReLU -> GAP -> softmax chain on [256,512,14,14]
-    # (BN in place on the depthwise output, ReLU in place, softmax over the
-    # 512 channels of each image), back to back on one stream after one L2
-    # flush; bytes: each kernel's input read once and output written once.
-    y2 = torch.empty_like(x)
-    sm_out = torch.empty(n * c, device=dev)
-    chain_bytes = (nx * 8 + w.numel() * 4) + nx * 8 + nx * 8 + (nx * 4 + n * c * 4) + n * c * 8
-
-    def chain():
-        # the same function tests/test_gpu_workloads.py checks against the
-        # reference's CPU chain
-        return abs(workloads.bandwidth_chain(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], y, y2,
-                                             gap, sm_out))
-
-    cases.append(("chain depthwise->BN->ReLU->GAP->softmax [256,512,14,14]", chain_bytes,
-                  chain))
     hbm, _, src = measured_peaks()
-    out = {}
-    # Size-matched reference: a device copy of the same 103 MB tensor (103 MB
-    # read + 103 MB written), timed the same way. Kernels of ~100 MB carry a
-    # fixed ramp-up and tail of several microseconds that the >= 1 GB copy
-    # behind the measured peak does not, so each kernel is also given as a
-    # fraction of this copy's rate.
-    copy_bytes = nx * 8
-    cases.append(("device copy of the same tensor (reference)", copy_bytes,
-                  lambda: (y.copy_(x), 0)[1]))
-    for name, nbytes, fn in cases:
-        assert fn() == 0
-        ts = []
-        for _ in range(reps):
-            flush()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
+
+    def cases_at(scale):
+        gen = torch.Generator(device=dev).manual_seed(0)
+        n, c, hw = 256 * scale, 512, 14
+        x = torch.randn(n, c, hw, hw, device=dev, generator=gen)
+        y = torch.empty_like(x)
+        w = torch.randn(c, 1, 3, 3, device=dev, generator=gen) * 0.3
+        bn = [torch.rand(c, device=dev, generator=gen) + 0.5 for _ in range(4)]
+        gap = torch.empty(n * c, device=dev)
+        pooled = torch.empty(n, c, 7, 7, device=dev)
+        rows = torch.randn(8192 * scale, 4096, device=dev, generator=gen)
+        rows_y = torch.empty_like(rows)
+        logits = torch.randn(102400 * scale, 1000, device=dev, generator=gen)
+        probs = torch.empty_like(logits)
+        g = nb.conv_geom(n, c, hw, hw, c, 3, 3, 1, 1)
+        nx = x.numel()
+        acc = torch.empty((), device=dev)
+        cases = [
+            ("depthwise 3x3", nx * 8 + w.numel() * 4,
+             lambda: lib.nplk_depthwise_conv2d(s, C.byref(g), p(x), p(w), None, p(y))),
+            ("batch_norm inference", nx * 8,
+             lambda: lib.nplk_batch_norm_infer(s, n, c, hw * hw, p(x), p(y), p(bn[0]), p(bn[1]),
+                                               p(bn[2]), p(bn[3]), 1e-5)),
+            ("relu", nx * 8, lambda: lib.nplk_activation(s, nx, p(x), p(y), 1, 0.0, 0)),
+            ("max pool 3x3/s2", nx * 4 + pooled.numel() * 4,
+             lambda: lib.nplk_pool2d(s, n, c, hw, hw, 3, 3, 2, 2, 1, 1, 7, 7, 0, 0, p(x),
+                                     p(pooled))),
+            ("global avg pool", nx * 4 + gap.numel() * 4,
+             lambda: lib.nplk_global_avg_pool(s, n * c, hw * hw, p(x), p(gap))),
+            ("softmax rows of 1000", logits.numel() * 8,
+             lambda: lib.nplk_softmax(s, logits.shape[0], 1000, 1, p(logits), p(probs))),
+            ("layer_norm 8192x4096", rows.numel() * 8,
+             lambda: lib.nplk_layer_norm(s, rows.shape[0], 4096, p(rows), p(rows_y), None, None,
+                                         1e-5)),
+        ]
+        if scale == 1:
+            # The depthwise -> BN -> ReLU -> GAP -> softmax chain on
+            # [256,512,14,14] (BN into a second tensor, ReLU in place, softmax
+            # over the 512 channels of each image), back to back after one L2
+            # flush; bytes: each kernel's input read once, output written once.
+            y2 = torch.empty_like(x)
+            sm_out = torch.empty(n * c, device=dev)
+            chain_bytes = (nx * 8 + w.numel() * 4) + nx * 8 + nx * 8 + (nx * 4 + n * c * 4) + \
+                n * c * 8
+
+            def chain():
+                # the same function tests/test_gpu_workloads.py checks against
+                # the reference's CPU chain
+                return abs(workloads.bandwidth_chain(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], y,
+                                                     y2, gap, sm_out))
+
+            cases.append(("chain depthwise->BN->ReLU->GAP->softmax [256,512,14,14]", chain_bytes,
+                          chain))
+        cases += [
+            ("device copy of the same tensor (reference)", nx * 8, lambda: (y.copy_(x), 0)[1]),
+            ("read (sum) of the same tensor (reference)", nx * 4,
+             lambda: (torch.sum(x.view(-1), dim=0, out=acc), 0)[1]),
+        ]
+        res = {}
+        for name, nbytes, fn in cases:
             assert fn() == 0
-            e1.record()
-            torch.cuda.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        ms = statistics.median(ts)
+            ts = []
+            for _ in range(reps):
+                flush()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                assert fn() == 0
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = statistics.median(ts)
+            res[name] = (ms, nbytes)
+        return res
+
+    out = {}
+    base = cases_at(1)
+    big = cases_at(4)
+    torch.cuda.empty_cache()
+    ref_gbs = None
+    for name, (ms, nbytes) in base.items():
         gbs = nbytes / (ms / 1e3) / 1e9
+        if name.startswith("device copy"):
+            ref_gbs = gbs
         out[name] = {"us": round(ms * 1e3, 1), "bytes": int(nbytes), "GB/s": round(gbs, 1),
                      "frac_of_hbm": round(gbs / hbm, 3)}
-    ref_gbs = out["device copy of the same tensor (reference)"]["GB/s"]
+        if name in big:
+            ms4, nb4 = big[name]
+            g4 = nb4 / (ms4 / 1e3) / 1e9
+            out[name].update({"us_4x": round(ms4 * 1e3, 1), "GB/s_4x": round(g4, 1),
+                              "frac_of_hbm_4x": round(g4 / hbm, 3)})
     for name, v in out.items():
         v["frac_of_copy_at_size"] = round(v["GB/s"] / ref_gbs, 3)
     out["peak"] = f"{src} HBM copy {hbm} GB/s (>= 1 GB transfers)"
+    out["sizes"] = ("at size: the workload's tensors; _4x: batch (rows) x4, outputs beyond L2 "
+                    "so their write-back falls inside the timed region")
     return out
 
 
@@ -715,8 +743,21 @@ def stem_also(lib, local_rank, reps=5):
         r = lib.nplk_pool2d(s, n, 64, 112, 112, 3, 3, 2, 2, 1, 1, 56, 56, 0, 0, p(y), p(pooled))
         assert r == 0, r
 
-    conv(), pool()
-    cms, pms = [], []
+    # The fused form: the conv epilogue writes the horizontal maxima of the
+    # pool windows (half the conv output) and a vertical pass finishes the
+    # pool (nplk_conv2d_maxpool_fused; bit-identical to conv then pool).
+    fws = lib.nplk_conv2d_maxpool_workspace_size(C.byref(g))
+    fwork = torch.empty(fws // 4 + 64, device=dev)
+    fused_out = torch.empty_like(pooled)
+
+    def fused():
+        r = lib.nplk_conv2d_maxpool_fused(s, C.byref(g), p(x), p(w), None, p(bn[0]), p(bn[1]),
+                                          p(bn[2]), p(bn[3]), 1e-5, nb.NPL_ACT_RELU, 0.0,
+                                          p(fused_out), p(fwork), fws, None)
+        assert r == 0, r
+
+    conv(), pool(), fused()
+    cms, pms, fms = [], [], []
     for _ in range(reps):
         flush()
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
@@ -728,14 +769,26 @@ def stem_also(lib, local_rank, reps=5):
         torch.cuda.synchronize()
         cms.append(e0.elapsed_time(e1))
         pms.append(e1.elapsed_time(e2))
+        flush()
+        e3, e4 = (torch.cuda.Event(enable_timing=True) for _ in range(2))
+        e3.record()
+        fused()
+        e4.record()
+        torch.cuda.synchronize()
+        fms.append(e3.elapsed_time(e4))
     if lib.nplk_read_status(s) != 0:
         raise RuntimeError("conv kernel reported a pipeline timeout")
+    same = bool(torch.equal(fused_out, pooled))
     flops = 2.0 * n * 64 * 3 * 112 * 112 * 49
-    cm, pm = statistics.median(cms), statistics.median(pms)
+    cm, pm, fm = statistics.median(cms), statistics.median(pms), statistics.median(fms)
     return {"workload": "conv 7x7/s2/p3 3->64 [128,3,224,224] + BN + ReLU, then max pool "
                         "3x3/s2/p1", "conv_ms": round(cm, 4),
             "conv_TFLOP/s": round(flops / (cm / 1e3) / 1e12, 2), "pool_ms": round(pm, 4),
-            "pool_GB/s": round((y.numel() + pooled.numel()) * 4 / (pm / 1e3) / 1e9, 1)}
+            "pool_GB/s": round((y.numel() + pooled.numel()) * 4 / (pm / 1e3) / 1e9, 1),
+            "conv_plus_pool_ms": round(cm + pm, 4),
+            "fused_conv_maxpool_ms": round(fm, 4),
+            "fused_TFLOP/s (conv flops)": round(flops / (fm / 1e3) / 1e12, 2),
+            "fused_output_identical": same}
 
 
 def gemm1024_also(lib, local_rank, reps=20):

@@ -186,6 +186,26 @@ NPL_API int nplk_conv2d_fused_noalloc(void *stream, const nplk_conv_geom_t *g, c
                                       const float *bn_beta, float bn_eps, int act,
                                       float act_alpha, float *out, int *status);
 
+/* Fused stem block: conv (+bias) (+inference BN) (+activation) followed by a
+ * 3x3 / stride 2 / pad 1 max pool (floor mode), the reference's
+ * npl_conv2d_bn_activation (npl_convolution.cpp:92-137) then npl_pooling
+ * max (npl_pooling.cpp:129-219). The conv epilogue writes only the
+ * horizontal maxima (half the conv output's bytes) and a vertical pass
+ * finishes the pool; the result is bit-identical to the two calls (same
+ * scan order, NaN skipped, first of equal values kept). `out` is
+ * [N][C_out][(H_out-1)/2+1][W_out/2]. Applies when the conv runs on the
+ * direct kernel's row order (C_in not a multiple of 32, filter rows of 3..8
+ * columns), C_out <= 64 and W_out is even; otherwise the size query returns
+ * 0 and the call NPL_ERR_UNSUPPORTED. The workspace holds the conv's
+ * weights and constants plus the horizontal maxima. */
+NPL_API size_t nplk_conv2d_maxpool_workspace_size(const nplk_conv_geom_t *g);
+NPL_API int nplk_conv2d_maxpool_fused(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                      const float *w, const float *bias, const float *bn_mean,
+                                      const float *bn_var, const float *bn_gamma,
+                                      const float *bn_beta, float bn_eps, int act,
+                                      float act_alpha, float *out, void *workspace,
+                                      size_t workspace_bytes, int *status);
+
 /* ---- bandwidth-bound primitives -------------------------------------------- */
 
 /* Depthwise conv, weights [C,1,kh,kw]; g->c_out must equal g->c_in. Dilation

@@ -144,6 +144,105 @@ __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t
   return true;
 }
 
+// Conv -> 3x3/s2/p1 max pool fusion (nplk_conv2d_maxpool_fused): instead of
+// the conv output y, the epilogue writes the horizontal maxima
+//   h[n][co][oh][pw] = max over ow in {2pw-1, 2pw, 2pw+1} of y[n][co][oh][ow]
+// (half of y's bytes), and a vertical pass takes the maximum over rows
+// {2ph-1, 2ph, 2ph+1}. Both passes scan in the reference's order with
+// "replace when greater" from -inf (ExecuteMaxPooling, npl_pooling.cpp:
+// 129-219), so NaNs are skipped and the first of equal values (+0 / -0) is
+// kept, exactly as the 3x3 scan does. Requires an even Wo (pairs of columns
+// never straddle a warp) and rows of the GEMM = output pixels (n, oh, ow).
+// The left neighbour (2pw-1) of a tile's first pixel belongs to the previous
+// tile: that h is written without it, and the previous tile's last pixel is
+// saved in e[tile][co] for the vertical pass to fold in.
+struct HmaxOut {
+  float *h;  // [N][Cout][Ho][wp]
+  float *e;  // [m_blocks][Cout]: each tile's last pixel
+  int wp;    // Wo / 2
+};
+struct NoHmax {};
+
+// Folds value `v` into a running maximum the reference's way.
+__device__ __forceinline__ float pool_max_step(float m, float v) { return v > m ? v : m; }
+
+// conv_epilogue_tile for the fused max pool: same accumulator drain, BN and
+// activation, then the horizontal maxima to f.h. `xch` is 128 floats of
+// shared memory (each warp's last lane, for the next warp's first lane).
+template <int BNC, int kAct>
+__device__ __forceinline__ bool conv_epilogue_tile_hmax(const ConvParams &p, uint32_t acc_tmem,
+                                                        int quad, int lane, int et, int mb,
+                                                        int nb, float4 *ep_s, float *ep_beta_s,
+                                                        uint64_t *acc_full, uint32_t acc_phase,
+                                                        volatile int *abort_flag,
+                                                        const HmaxOut &f, float *xch) {
+  mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
+  named_barrier_sync(1, 128);
+  if (*abort_flag) return false;
+  for (int i = et; i < BNC; i += 128) {
+    const int co = nb * BNC + i;
+    ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
+                          p.ep[kEpGamma * p.cout_pad + co], p.ep[kEpInvStd * p.cout_pad + co]);
+    ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
+  }
+  named_barrier_sync(1, 128);
+  tc_fence_after_sync();
+  const int m = mb * kConvBM + quad * 32 + lane;  // GEMM row = output pixel
+  const bool valid = m < p.M;
+  int n = 0, oh = 0, ow = 0;
+  if (valid) {
+    n = m / static_cast<int>(p.HoWo);
+    const int pix = m - n * static_cast<int>(p.HoWo);
+    oh = pix / p.Wo;
+    ow = pix - oh * p.Wo;
+  }
+  // Even columns are pool centres; their right neighbour is lane + 1 (same
+  // row, Wo even). The left one is lane - 1, the previous warp's last lane
+  // for lane 0, or (lane 0 of the tile's first warp) in the previous tile.
+  const bool centre = valid && (ow & 1) == 0;
+  const bool has_left = ow > 0 && (lane > 0 || quad > 0);
+  float *hrow = f.h + (static_cast<int64_t>(n) * p.Cout * p.Ho + oh) * f.wp + (ow >> 1);
+  const int64_t hplane = static_cast<int64_t>(p.Ho) * f.wp;
+  const uint32_t t_row = acc_tmem + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BNC; c0 += 32) {
+    uint32_t v[32], w[32];
+    tmem_ld32(t_row + c0, v);
+    tmem_ld32(t_row + BNC + c0, w);
+    tmem_wait_ld2(v, w);
+    const int co0 = nb * BNC + c0;
+    float out[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float4 c = ep_s[c0 + j];
+      float t = (__uint_as_float(v[j]) + __uint_as_float(w[j])) + c.x;
+      t = c.z * (t - c.y) * c.w + ep_beta_s[c0 + j];
+      out[j] = epilogue_act<kAct>(t, p.act, p.act_alpha);
+    }
+    if (lane == 31) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) xch[quad * 32 + j] = out[j];
+      if (quad == 3 && valid)
+        for (int j = 0; j < 32 && co0 + j < p.Cout; ++j)
+          f.e[static_cast<int64_t>(mb) * p.Cout + co0 + j] = out[j];
+    }
+    named_barrier_sync(2, 128);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float left = __shfl_up_sync(0xffffffffu, out[j], 1);
+      const float right = __shfl_down_sync(0xffffffffu, out[j], 1);
+      if (lane == 0 && quad > 0) left = xch[(quad - 1) * 32 + j];
+      float mx = -__int_as_float(0x7f800000);
+      if (has_left) mx = pool_max_step(mx, left);
+      mx = pool_max_step(mx, out[j]);
+      mx = pool_max_step(mx, right);
+      if (centre && co0 + j < p.Cout) hrow[static_cast<int64_t>(co0 + j) * hplane] = mx;
+    }
+    named_barrier_sync(2, 128);  // xch is rewritten by the next chunk
+  }
+  return true;
+}
+
 // Launches the TMA-im2col conv (conv_im2col.cu) for channel counts that are a
 // multiple of 32: x_hi / x_lo are the input's NHWC tf32 hi/lo planes written
 // by launch_nchw_to_nhwc_split. Returns an NPL error code.

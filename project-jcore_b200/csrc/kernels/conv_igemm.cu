@@ -38,6 +38,7 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 #include <vector>
 
 #include "conv_common.cuh"
@@ -63,7 +64,8 @@ struct ConvTraits {
   static constexpr int kAccCols = 2 * BNC;
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kSmemBytes =
-      1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20;  // + epilogue constants
+      1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20  // + epilogue constants
+      + 512;  // + the fused max pool's warp-boundary exchange (conv_epilogue_tile_hmax)
 };
 
 // k orders of the direct kernel (4 and 8 are the row order's slot counts).
@@ -83,9 +85,12 @@ inline int conv_row_slots(int64_t C, int64_t KW, int64_t dw) {
 // consecutive channels and the gather needs no per-element tap bookkeeping;
 // 4 or 8 -- row order with that many slots per filter row; kModeTaps --
 // tap-major, any geometry.
-template <int BNC, int kMode, int kAct>
+// Fuse: NoHmax (the conv output y) or HmaxOut (the fused max pool's
+// horizontal maxima instead, conv_epilogue_tile_hmax).
+template <int BNC, int kMode, int kAct, class Fuse>
 __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
-    conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p) {
+    conv_igemm_3xtf32_kernel(const __grid_constant__ CUtensorMap map_w, const ConvParams p,
+                             const __grid_constant__ Fuse fz) {
   using T = ConvTraits<BNC>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = align_smem_1024(smem_raw);
@@ -99,6 +104,7 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   float4 *ep_s = reinterpret_cast<float4 *>(smem_b + T::kStages * T::kBStageBytes + 256);
   float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
+  float *xch = ep_beta_s + BNC;  // 128 floats (fused max pool only)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -348,9 +354,16 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       const int mb = tile / p.n_blocks;
       const int nb = tile - mb * p.n_blocks;
-      if (!conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb, nb,
-                                         ep_s, ep_beta_s, &acc_full[acc], acc_phase, abort_flag))
-        break;
+      bool ok;
+      if constexpr (std::is_same<Fuse, HmaxOut>::value)
+        ok = conv_epilogue_tile_hmax<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et,
+                                                mb, nb, ep_s, ep_beta_s, &acc_full[acc],
+                                                acc_phase, abort_flag, fz, xch);
+      else
+        ok = conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb,
+                                           nb, ep_s, ep_beta_s, &acc_full[acc], acc_phase,
+                                           abort_flag);
+      if (!ok) break;
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -545,19 +558,22 @@ ConvPlan plan_conv(const nplk_conv_geom_t *g, int algo = NPLK_CONV_ALGO_AUTO,
   return c;
 }
 
-template <int BNC, int kMode, int kAct>
-int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
+template <int BNC, int kMode, int kAct, class Fuse = NoHmax>
+int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm,
+                const Fuse &fz = Fuse{}) {
   using T = ConvTraits<BNC>;
   CUtensorMap map_w;
   int rc = encode_tmap_2d_f32_sw128(&map_w, wsplit, c.kp, c.n_blocks * 2 * BNC, c.kp * 4,
                                     kConvBK, 2 * BNC);
   if (rc) return rc;
   rc = ensure_dynamic_smem(
-      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kMode, kAct>), T::kSmemBytes);
+      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse>),
+      T::kSmemBytes);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_igemm_3xtf32_kernel<BNC, kMode, kAct><<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm);
+  conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse>
+      <<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm, fz);
   count_launch();
   return launch_result();
 }
@@ -876,5 +892,132 @@ extern "C" int nplk_conv2d_tune(void *stream, const nplk_conv_geom_t *g, const f
   *best_algo = best;
   if (best_us) *best_us = best_ms * 1000.0f;
   return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// conv -> 3x3/s2/p1 max pool, fused through the horizontal-max epilogue
+// (conv_epilogue_tile_hmax) and a vertical pass. Replaces the reference's
+// stem sequence of npl_conv2d_bn_activation (npl_convolution.cpp:92-137) and
+// npl_pooling max 3x3/s2/p1 (npl_pooling.cpp:129-219) for geometries the
+// direct kernel's row order serves (C_in not a multiple of 32, filter rows of
+// 3..8 columns), C_out <= 64 and an even output width.
+// ---------------------------------------------------------------------------
+namespace nplk {
+namespace {
+
+// out[n][c][ph][pw] = max over rows {2ph-1, 2ph, 2ph+1} of h[n][c][row][pw]
+// in the reference's scan order; where h lacks its left neighbour (the
+// centre is the first pixel of a GEMM tile) the previous tile's last pixel
+// e[tile-1][c] is folded in first.
+__global__ void pool_vmax_kernel(const float *__restrict__ h, const float *__restrict__ e,
+                                 float *__restrict__ out, int64_t total, int C, int Ho, int Wo,
+                                 int wp, int po) {
+  const float ninf = -__int_as_float(0x7f800000);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int pw = static_cast<int>(i % wp);
+    int64_t r = i / wp;
+    const int ph = static_cast<int>(r % po);
+    r /= po;
+    const int c = static_cast<int>(r % C);
+    const int64_t n = r / C;
+    const float *hp = h + (n * C + c) * static_cast<int64_t>(Ho) * wp + pw;
+    float mx = ninf;
+#pragma unroll
+    for (int dr = -1; dr <= 1; ++dr) {
+      const int row = 2 * ph + dr;
+      if (row < 0 || row >= Ho) continue;
+      float v = hp[static_cast<int64_t>(row) * wp];
+      const int64_t pix = (n * Ho + row) * Wo + 2 * pw;  // GEMM row of the centre
+      if (pw > 0 && (pix & (kConvBM - 1)) == 0)
+        v = pool_max_step(pool_max_step(ninf, e[(pix / kConvBM - 1) * C + c]), v);
+      mx = pool_max_step(mx, v);
+    }
+    out[i] = mx;
+  }
+}
+
+struct PoolFusePlan {
+  ConvPlan c;
+  int64_t wp, po, m_blocks;
+  size_t h_bytes, e_bytes;
+  bool ok;
+};
+
+PoolFusePlan plan_pool_fuse(const nplk_conv_geom_t *g) {
+  PoolFusePlan f{};
+  if (validate_conv_geom(g) != kOk) return f;
+  f.c = plan_conv(g, NPLK_CONV_ALGO_DIRECT, false);
+  f.ok = f.c.bnc == 64 && f.c.n_blocks == 1 && (f.c.mode == 4 || f.c.mode == 8) &&
+         g->w_out % 2 == 0 && g->w_out >= 2 && g->h_out >= 1;
+  f.wp = g->w_out / 2;                // floor((Wo + 2 - 3) / 2) + 1 for even Wo
+  f.po = (g->h_out - 1) / 2 + 1;     // floor((Ho + 2 - 3) / 2) + 1
+  f.m_blocks = ceil_div(g->n * g->h_out * g->w_out, kConvBM);
+  f.h_bytes = align_up(static_cast<size_t>(g->n * g->c_out * g->h_out * f.wp) * 4, 256);
+  f.e_bytes = align_up(static_cast<size_t>(f.m_blocks * g->c_out) * 4, 256);
+  return f;
+}
+
+template <int kMode>
+int launch_hmax(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm,
+                const HmaxOut &fz) {
+  if (prm.act == 1) return launch_conv<64, kMode, kEpiActRelu>(s, c, wsplit, prm, fz);
+  return launch_conv<64, kMode, kEpiActAny>(s, c, wsplit, prm, fz);
+}
+
+}  // namespace
+}  // namespace nplk
+
+extern "C" size_t nplk_conv2d_maxpool_workspace_size(const nplk_conv_geom_t *g) {
+  const PoolFusePlan f = plan_pool_fuse(g);
+  if (!f.ok) return 0;
+  return f.c.min_bytes() + f.h_bytes + f.e_bytes;
+}
+
+extern "C" int nplk_conv2d_maxpool_fused(void *stream, const nplk_conv_geom_t *g,
+                                         const float *x, const float *w, const float *bias,
+                                         const float *bn_mean, const float *bn_var,
+                                         const float *bn_gamma, const float *bn_beta,
+                                         float bn_eps, int act, float act_alpha, float *out,
+                                         void *workspace, size_t workspace_bytes, int *status) {
+  if (!g || !x || !w || !out) return kErrInvalidArg;
+  const PoolFusePlan f = plan_pool_fuse(g);
+  if (!f.ok) return kErrUnsupported;
+  const size_t need = f.c.min_bytes() + f.h_bytes + f.e_bytes;
+  if (!workspace || workspace_bytes < need ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return kErrInvalidArg;
+  int rc = nplk_conv2d_prepare(stream, g, w, bias, bn_mean, bn_var, bn_gamma, bn_beta, bn_eps,
+                               workspace, workspace_bytes);
+  if (rc) return rc;
+  if (!status) status = device_status_word();
+  if (!status) return kErrInternal;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ConvParams prm = conv_params(g, f.c);
+  prm.x = x;
+  prm.y = nullptr;  // the epilogue writes the horizontal maxima instead
+  prm.ep = reinterpret_cast<const float *>(static_cast<const uint8_t *>(workspace) + f.c.w_bytes);
+  prm.act = act;
+  prm.act_alpha = act_alpha;
+  prm.status = status;
+  uint8_t *base = static_cast<uint8_t *>(workspace) + f.c.min_bytes();
+  HmaxOut fz;
+  fz.h = reinterpret_cast<float *>(base);
+  fz.e = reinterpret_cast<float *>(base + f.h_bytes);
+  fz.wp = static_cast<int>(f.wp);
+  const float *wsplit = static_cast<const float *>(workspace);
+  rc = f.c.mode == 8 ? launch_hmax<8>(s, f.c, wsplit, prm, fz)
+                     : launch_hmax<4>(s, f.c, wsplit, prm, fz);
+  if (rc) return rc;
+  const int64_t total = g->n * g->c_out * f.po * f.wp;
+  const int threads = 256;
+  const int64_t want = ceil_div(total, threads);
+  const int blocks = static_cast<int>(want < 8 * 148 * 8 ? want : 8 * 148 * 8);
+  pool_vmax_kernel<<<blocks, threads, 0, s>>>(fz.h, fz.e, out, total, static_cast<int>(g->c_out),
+                                              static_cast<int>(g->h_out),
+                                              static_cast<int>(g->w_out), fz.wp,
+                                              static_cast<int>(f.po));
+  count_launch();
+  return launch_result();
 }
 

@@ -183,6 +183,9 @@ NPLK_SIGNATURES = {
     "nplk_conv2d_run_staged": (C.c_int, [_VP, _G, C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_conv2d_fused_noalloc": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
                                             C.c_int, _F, _VP, _VP]),
+    "nplk_conv2d_maxpool_workspace_size": (C.c_size_t, [_G]),
+    "nplk_conv2d_maxpool_fused": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
+                                            C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_depthwise_conv2d": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP]),
     "nplk_batch_norm_infer": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _F]),
     "nplk_batch_norm_stats": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP]),

@@ -12,6 +12,10 @@ and checks the kernel status word.
     python -m npl_b200.profile_cases layernorm # 8192 x 16384 rows
     python -m npl_b200.profile_cases pool      # max pool 3x3/s2 [32,64,112,112] -> 56x56
     python -m npl_b200.profile_cases gemm_raw  # the 4096x4096x8192 GEMM, raw operand form
+    python -m npl_b200.profile_cases gemm_1024 # 1024^3 (split kernels + GEMM)
+    python -m npl_b200.profile_cases bandwidth # BN, ReLU, GAP on 256x512x14x14; softmax 102400x1000
+    python -m npl_b200.profile_cases allgather # fused GEMM all-gather epilogue, 2 simulated ranks
+    python -m npl_b200.profile_cases conv_pair # the 3x3 conv on CTA pairs
 
 Run from the package directory (``project-jcore_b200``) or with it on sys.path.
 """
@@ -119,6 +123,54 @@ def case_layernorm(reps: int = 3):
     torch.cuda.synchronize()
 
 
+def case_bandwidth(reps: int = 2):
+    """Batch norm (inference), ReLU and global average pool on [256,512,14,14]
+    (103 MB) and softmax over 102400 rows of 1000 (410 MB), `reps` rounds in
+    that order."""
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    n, c, hw = 256, 512, 14
+    x = torch.randn(n, c, hw, hw, device="cuda", generator=gen)
+    y = torch.empty_like(x)
+    bn = [torch.rand(c, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    gap = torch.empty(n * c, device="cuda")
+    logits = torch.randn(102400, 1000, device="cuda", generator=gen)
+    probs = torch.empty_like(logits)
+    for _ in range(reps):
+        assert lib.nplk_batch_norm_infer(s, n, c, hw * hw, _p(x), _p(y), _p(bn[0]), _p(bn[1]),
+                                         _p(bn[2]), _p(bn[3]), 1e-5) == 0
+        assert lib.nplk_activation(s, x.numel(), _p(x), _p(y), 1, 0.0, 0) == 0
+        assert lib.nplk_global_avg_pool(s, n * c, hw * hw, _p(x), _p(gap)) == 0
+        assert lib.nplk_softmax(s, 102400, 1000, 1, _p(logits), _p(probs)) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+
+
+def case_allgather(reps: int = 2, m: int = 4096, n_local: int = 2048, k: int = 4096,
+                   ranks: int = 2):
+    """The fused GEMM + all-gather epilogue (nplk_gemm_allgather) with `ranks`
+    simulated ranks on one GPU: every output tile is stored into `ranks` full
+    row-major C buffers (on this device), as the multi-GPU form stores into
+    every rank's C; then the NCCL form's relayout kernel on [ranks][m][n_local]."""
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    a = torch.randn(m, k, device="cuda", generator=gen)
+    b = torch.randn(k, n_local, device="cuda", generator=gen) / 64.0
+    cs = [torch.empty(m, ranks * n_local, device="cuda") for _ in range(ranks)]
+    dst = (C.c_void_p * ranks)(*[t.data_ptr() for t in cs])
+    ws = lib.nplk_gemm_workspace_size(m, n_local, k)
+    work = torch.empty(ws // 4 + 64, device="cuda")
+    blocks = torch.randn(ranks * m * n_local, device="cuda", generator=gen)
+    out = torch.empty(m, ranks * n_local, device="cuda")
+    for _ in range(reps):
+        rc = lib.nplk_gemm_allgather(s, m, n_local, k, 1.0, _p(a), k, _p(b), n_local, None, 0,
+                                     0.0, dst, ranks, 0, ranks * n_local, 0, _p(work), ws, None)
+        assert rc == 0, rc
+        assert lib.nplk_colshard_relayout(s, ranks, m, n_local, _p(blocks), _p(out)) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+
+
 CASES = {"conv": case_conv,
          "conv_direct": lambda: case_conv(algo=1),
          "conv_window_tma": lambda: case_conv(algo=3),
@@ -126,7 +178,9 @@ CASES = {"conv": case_conv,
          "stem": case_stem, "gemm": case_gemm, "chain": case_chain,
          "layernorm": case_layernorm, "pool": case_pool,
          "gemm_raw": lambda: case_gemm(raw=True),
-         "gemm_1024": lambda: case_gemm(m=1024, n=1024, k=1024)}
+         "gemm_1024": lambda: case_gemm(m=1024, n=1024, k=1024),
+         "bandwidth": case_bandwidth, "allgather": case_allgather,
+         "conv_pair": lambda: case_conv(algo=5)}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else "conv"
