@@ -195,7 +195,7 @@ NPL_API int nplk_conv2d_fused_noalloc(void *stream, const nplk_conv_geom_t *g, c
  * scan order, NaN skipped, first of equal values kept). `out` is
  * [N][C_out][(H_out-1)/2+1][W_out/2]. Applies when the conv runs on the
  * direct kernel's row order (C_in not a multiple of 32, filter rows of 3..8
- * columns), C_out <= 64 and W_out is even; otherwise the size query returns
+ * columns), C_out <= 64 and W_out is even and >= 32; otherwise the size query returns
  * 0 and the call NPL_ERR_UNSUPPORTED. The workspace holds the conv's
  * weights and constants plus the horizontal maxima. */
 NPL_API size_t nplk_conv2d_maxpool_workspace_size(const nplk_conv_geom_t *g);
@@ -301,8 +301,11 @@ NPL_API int nplk_ipc_close_handle(void *dev_ptr, uint64_t offset);
  * with nplk_ipc_open_handle -- at columns col_offset .. col_offset + N_local, so
  * the exchange crosses NVLink tile by tile while the GEMM runs and every rank
  * ends with the whole row-major C once all ranks' kernels have completed. `dst`
- * is a host array of device addresses valid on the current device. beta is 0
- * (C is not read); other arguments as nplk_gemm. */
+ * is a host array of device addresses valid on the current device. With the
+ * usual layout (dst[] in rank order, col_offset = rank * N_local) each rank
+ * visits the destinations starting after its own index, so the ranks' stores
+ * spread over all peers instead of converging on one; any order gives the
+ * same C. beta is 0 (C is not read); other arguments as nplk_gemm. */
 NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
                                 float alpha, const float *A, int64_t lda, const float *B,
                                 int64_t ldb, const float *bias, int act, float act_alpha,

@@ -152,13 +152,15 @@ __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t
 // "replace when greater" from -inf (ExecuteMaxPooling, npl_pooling.cpp:
 // 129-219), so NaNs are skipped and the first of equal values (+0 / -0) is
 // kept, exactly as the 3x3 scan does. Requires an even Wo (pairs of columns
-// never straddle a warp) and rows of the GEMM = output pixels (n, oh, ow).
-// The left neighbour (2pw-1) of a tile's first pixel belongs to the previous
-// tile: that h is written without it, and the previous tile's last pixel is
-// saved in e[tile][co] for the vertical pass to fold in.
+// never straddle a 32-pixel group) and GEMM rows = output pixels
+// (n, oh, ow). Each warp holds 32 consecutive pixels; the left neighbour
+// (2pw-1) of a group's first pixel belongs to the previous group, so that h
+// is written without it and every group's last pixel is saved in
+// e[group][co] for the vertical pass to fold in (no exchange between warps).
+constexpr int kHmaxGroup = 32;  // pixels per warp
 struct HmaxOut {
   float *h;  // [N][Cout][Ho][wp]
-  float *e;  // [m_blocks][Cout]: each tile's last pixel
+  float *e;  // [ceil(M / 32)][Cout]: each 32-pixel group's last pixel
   int wp;    // Wo / 2
 };
 struct NoHmax {};
@@ -166,16 +168,24 @@ struct NoHmax {};
 // Folds value `v` into a running maximum the reference's way.
 __device__ __forceinline__ float pool_max_step(float m, float v) { return v > m ? v : m; }
 
+// Per-warp staging block of the fused max pool's epilogue: 32 pixels x 32
+// channels, row pitch 36 floats (16-byte aligned rows, conflict-free float4
+// stores and column reads).
+constexpr int kHmaxPitch = 36;
+constexpr int kHmaxStageBytes = 4 * 32 * kHmaxPitch * 4;
+
 // conv_epilogue_tile for the fused max pool: same accumulator drain, BN and
-// activation, then the horizontal maxima to f.h. `xch` is 128 floats of
-// shared memory (each warp's last lane, for the next warp's first lane).
+// activation; each warp then stages its 32 pixels x 32 channels in shared
+// memory (`stg`, this warp's block) and reads it back transposed, so that
+// lane l scans channel l along the 32 pixels and writes that channel's 16
+// horizontal maxima (float4 stores where the row segment allows).
 template <int BNC, int kAct>
 __device__ __forceinline__ bool conv_epilogue_tile_hmax(const ConvParams &p, uint32_t acc_tmem,
                                                         int quad, int lane, int et, int mb,
                                                         int nb, float4 *ep_s, float *ep_beta_s,
                                                         uint64_t *acc_full, uint32_t acc_phase,
                                                         volatile int *abort_flag,
-                                                        const HmaxOut &f, float *xch) {
+                                                        const HmaxOut &f, float *stg) {
   mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
   named_barrier_sync(1, 128);
   if (*abort_flag) return false;
@@ -187,30 +197,27 @@ __device__ __forceinline__ bool conv_epilogue_tile_hmax(const ConvParams &p, uin
   }
   named_barrier_sync(1, 128);
   tc_fence_after_sync();
-  const int m = mb * kConvBM + quad * 32 + lane;  // GEMM row = output pixel
-  const bool valid = m < p.M;
-  int n = 0, oh = 0, ow = 0;
-  if (valid) {
-    n = m / static_cast<int>(p.HoWo);
-    const int pix = m - n * static_cast<int>(p.HoWo);
-    oh = pix / p.Wo;
-    ow = pix - oh * p.Wo;
-  }
-  // Even columns are pool centres; their right neighbour is lane + 1 (same
-  // row, Wo even). The left one is lane - 1, the previous warp's last lane
-  // for lane 0, or (lane 0 of the tile's first warp) in the previous tile.
-  const bool centre = valid && (ow & 1) == 0;
-  const bool has_left = ow > 0 && (lane > 0 || quad > 0);
-  float *hrow = f.h + (static_cast<int64_t>(n) * p.Cout * p.Ho + oh) * f.wp + (ow >> 1);
-  const int64_t hplane = static_cast<int64_t>(p.Ho) * f.wp;
+  // The warp's 32 pixels g0 .. g0+31 (warp-uniform): first pixel (n0, oh0,
+  // ow0); pixel b (even, since g0 and Wo are even) starts the next output
+  // row when b < 32; pixels from `nvalid` on lie past the last one.
+  const int g0 = mb * kConvBM + quad * 32;
+  const int n0 = g0 / static_cast<int>(p.HoWo);
+  const int r0 = g0 - n0 * static_cast<int>(p.HoWo);
+  const int oh0 = r0 / p.Wo;
+  const int ow0 = r0 - oh0 * p.Wo;
+  const int b = p.Wo - ow0;  // >= 32: one row
+  const int n1 = oh0 + 1 == p.Ho ? n0 + 1 : n0;
+  const int oh1 = oh0 + 1 == p.Ho ? 0 : oh0 + 1;
+  const int nvalid = p.M - g0 < 32 ? p.M - g0 : 32;
+  const bool vec = b >= 32 && nvalid == 32 && ((ow0 >> 1) & 3) == 0 && (f.wp & 3) == 0;
   const uint32_t t_row = acc_tmem + (static_cast<uint32_t>(quad * 32) << 16);
+  const float ninf = -__int_as_float(0x7f800000);
 #pragma unroll 1
   for (int c0 = 0; c0 < BNC; c0 += 32) {
     uint32_t v[32], w[32];
     tmem_ld32(t_row + c0, v);
     tmem_ld32(t_row + BNC + c0, w);
     tmem_wait_ld2(v, w);
-    const int co0 = nb * BNC + c0;
     float out[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
@@ -219,26 +226,50 @@ __device__ __forceinline__ bool conv_epilogue_tile_hmax(const ConvParams &p, uin
       t = c.z * (t - c.y) * c.w + ep_beta_s[c0 + j];
       out[j] = epilogue_act<kAct>(t, p.act, p.act_alpha);
     }
-    if (lane == 31) {
+    float4 *s4 = reinterpret_cast<float4 *>(stg + lane * kHmaxPitch);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) xch[quad * 32 + j] = out[j];
-      if (quad == 3 && valid)
-        for (int j = 0; j < 32 && co0 + j < p.Cout; ++j)
-          f.e[static_cast<int64_t>(mb) * p.Cout + co0 + j] = out[j];
-    }
-    named_barrier_sync(2, 128);
+    for (int q = 0; q < 8; ++q)
+      s4[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+    __syncwarp();
+    float col[32];  // channel co0 + lane along the 32 pixels
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float left = __shfl_up_sync(0xffffffffu, out[j], 1);
-      const float right = __shfl_down_sync(0xffffffffu, out[j], 1);
-      if (lane == 0 && quad > 0) left = xch[(quad - 1) * 32 + j];
-      float mx = -__int_as_float(0x7f800000);
-      if (has_left) mx = pool_max_step(mx, left);
-      mx = pool_max_step(mx, out[j]);
-      mx = pool_max_step(mx, right);
-      if (centre && co0 + j < p.Cout) hrow[static_cast<int64_t>(co0 + j) * hplane] = mx;
+    for (int q = 0; q < 32; ++q) col[q] = stg[q * kHmaxPitch + lane];
+    __syncwarp();  // the next chunk rewrites the block
+    float hm[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+      const int pc = 2 * q;  // centre pixel within the group
+      float mx = ninf;
+      // left neighbour in the group unless the centre starts a row (the
+      // group's first pixel takes it from e in the vertical pass)
+      if (pc > 0 && pc != b) mx = pool_max_step(mx, col[pc - 1]);
+      mx = pool_max_step(mx, col[pc]);
+      mx = pool_max_step(mx, col[pc + 1]);
+      hm[q] = mx;
     }
-    named_barrier_sync(2, 128);  // xch is rewritten by the next chunk
+    const int co = nb * BNC + c0 + lane;
+    if (co < p.Cout) {
+      float *ha = f.h + ((static_cast<int64_t>(n0) * p.Cout + co) * p.Ho + oh0) * f.wp + (ow0 >> 1);
+      if (vec) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<float4 *>(ha)[q] =
+              make_float4(hm[4 * q], hm[4 * q + 1], hm[4 * q + 2], hm[4 * q + 3]);
+      } else {
+        float *hb = f.h + ((static_cast<int64_t>(n1) * p.Cout + co) * p.Ho + oh1) * f.wp;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const int pc = 2 * q;
+          if (pc >= nvalid) break;
+          if (pc < b)
+            ha[q] = hm[q];
+          else
+            hb[(pc - b) >> 1] = hm[q];
+        }
+      }
+      // The group's last pixel, for the next group's first centre.
+      if (nvalid == 32) f.e[static_cast<int64_t>(g0 / kHmaxGroup) * p.Cout + co] = col[31];
+    }
   }
   return true;
 }

@@ -64,8 +64,7 @@ struct ConvTraits {
   static constexpr int kAccCols = 2 * BNC;
   static constexpr int kTmemCols = 2 * kAccCols;
   static constexpr int kSmemBytes =
-      1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20  // + epilogue constants
-      + 512;  // + the fused max pool's warp-boundary exchange (conv_epilogue_tile_hmax)
+      1024 + kStages * (kAStageBytes + kBStageBytes) + 256 + BNC * 20;  // + epilogue constants
 };
 
 // k orders of the direct kernel (4 and 8 are the row order's slot counts).
@@ -104,7 +103,6 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   float4 *ep_s = reinterpret_cast<float4 *>(smem_b + T::kStages * T::kBStageBytes + 256);
   float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
-  float *xch = ep_beta_s + BNC;  // 128 floats (fused max pool only)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -356,9 +354,10 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
       const int nb = tile - mb * p.n_blocks;
       bool ok;
       if constexpr (std::is_same<Fuse, HmaxOut>::value)
-        ok = conv_epilogue_tile_hmax<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et,
-                                                mb, nb, ep_s, ep_beta_s, &acc_full[acc],
-                                                acc_phase, abort_flag, fz, xch);
+        ok = conv_epilogue_tile_hmax<BNC, kAct>(
+            p, tmem_base + acc * T::kAccCols, quad, lane, et, mb, nb, ep_s, ep_beta_s,
+            &acc_full[acc], acc_phase, abort_flag, fz,
+            reinterpret_cast<float *>(ep_beta_s + BNC) + quad * 32 * kHmaxPitch);
       else
         ok = conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb,
                                            nb, ep_s, ep_beta_s, &acc_full[acc], acc_phase,
@@ -566,14 +565,15 @@ int launch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvPara
   int rc = encode_tmap_2d_f32_sw128(&map_w, wsplit, c.kp, c.n_blocks * 2 * BNC, c.kp * 4,
                                     kConvBK, 2 * BNC);
   if (rc) return rc;
+  // The fused max pool's epilogue stages 32 x 32 blocks after the epilogue
+  // constants.
+  const int smem = T::kSmemBytes + (std::is_same<Fuse, HmaxOut>::value ? kHmaxStageBytes : 0);
   rc = ensure_dynamic_smem(
-      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse>),
-      T::kSmemBytes);
+      reinterpret_cast<const void *>(conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse>), smem);
   if (rc) return rc;
   const int64_t tiles = static_cast<int64_t>(prm.m_blocks) * prm.n_blocks;
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
-  conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse>
-      <<<grid, T::kThreads, T::kSmemBytes, s>>>(map_w, prm, fz);
+  conv_igemm_3xtf32_kernel<BNC, kMode, kAct, Fuse><<<grid, T::kThreads, smem, s>>>(map_w, prm, fz);
   count_launch();
   return launch_result();
 }
@@ -907,33 +907,56 @@ namespace {
 
 // out[n][c][ph][pw] = max over rows {2ph-1, 2ph, 2ph+1} of h[n][c][row][pw]
 // in the reference's scan order; where h lacks its left neighbour (the
-// centre is the first pixel of a GEMM tile) the previous tile's last pixel
-// e[tile-1][c] is folded in first.
+// centre is the first pixel of a 32-pixel group) the previous group's last
+// pixel e[group-1][c] is folded in first. Grid: y over (n, c) planes, x over the
+// plane's outputs, kV consecutive columns per thread (float4 when wp % 4 == 0).
+template <int kV>
 __global__ void pool_vmax_kernel(const float *__restrict__ h, const float *__restrict__ e,
-                                 float *__restrict__ out, int64_t total, int C, int Ho, int Wo,
+                                 float *__restrict__ out, int64_t planes, int C, int Ho, int Wo,
                                  int wp, int po) {
   const float ninf = -__int_as_float(0x7f800000);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int pw = static_cast<int>(i % wp);
-    int64_t r = i / wp;
-    const int ph = static_cast<int>(r % po);
-    r /= po;
-    const int c = static_cast<int>(r % C);
-    const int64_t n = r / C;
-    const float *hp = h + (n * C + c) * static_cast<int64_t>(Ho) * wp + pw;
-    float mx = ninf;
+  const int wq = wp / kV;
+  const int items = po * wq;
+  for (int64_t pl = blockIdx.y; pl < planes; pl += gridDim.y) {
+    const int c = static_cast<int>(static_cast<uint32_t>(pl) % static_cast<uint32_t>(C));
+    const int64_t n = static_cast<int64_t>(static_cast<uint32_t>(pl) / static_cast<uint32_t>(C));
+    const float *hp = h + pl * Ho * wp;
+    float *op = out + pl * po * wp;
+    for (int it = blockIdx.x * blockDim.x + threadIdx.x; it < items; it += gridDim.x * blockDim.x) {
+      const int ph = it / wq;
+      const int pw0 = (it - ph * wq) * kV;
+      float mx[kV];
 #pragma unroll
-    for (int dr = -1; dr <= 1; ++dr) {
-      const int row = 2 * ph + dr;
-      if (row < 0 || row >= Ho) continue;
-      float v = hp[static_cast<int64_t>(row) * wp];
-      const int64_t pix = (n * Ho + row) * Wo + 2 * pw;  // GEMM row of the centre
-      if (pw > 0 && (pix & (kConvBM - 1)) == 0)
-        v = pool_max_step(pool_max_step(ninf, e[(pix / kConvBM - 1) * C + c]), v);
-      mx = pool_max_step(mx, v);
+      for (int k = 0; k < kV; ++k) mx[k] = ninf;
+#pragma unroll
+      for (int dr = -1; dr <= 1; ++dr) {
+        const int row = 2 * ph + dr;
+        if (row < 0 || row >= Ho) continue;
+        float v[kV];
+        if constexpr (kV == 4) {
+          const float4 t = *reinterpret_cast<const float4 *>(hp + row * wp + pw0);
+          v[0] = t.x;
+          v[1] = t.y;
+          v[2] = t.z;
+          v[3] = t.w;
+        } else {
+          v[0] = hp[row * wp + pw0];
+        }
+        const int64_t base = (n * Ho + row) * Wo;  // GEMM row of the row's first pixel
+#pragma unroll
+        for (int k = 0; k < kV; ++k) {
+          const int pw = pw0 + k;
+          const int64_t pix = base + 2 * pw;  // GEMM row of the centre
+          if (pw > 0 && (pix & (kHmaxGroup - 1)) == 0)
+            v[k] = pool_max_step(pool_max_step(ninf, e[(pix / kHmaxGroup - 1) * C + c]), v[k]);
+          mx[k] = pool_max_step(mx[k], v[k]);
+        }
+      }
+      if constexpr (kV == 4)
+        *reinterpret_cast<float4 *>(op + ph * wp + pw0) = make_float4(mx[0], mx[1], mx[2], mx[3]);
+      else
+        op[ph * wp + pw0] = mx[0];
     }
-    out[i] = mx;
   }
 }
 
@@ -949,12 +972,13 @@ PoolFusePlan plan_pool_fuse(const nplk_conv_geom_t *g) {
   if (validate_conv_geom(g) != kOk) return f;
   f.c = plan_conv(g, NPLK_CONV_ALGO_DIRECT, false);
   f.ok = f.c.bnc == 64 && f.c.n_blocks == 1 && (f.c.mode == 4 || f.c.mode == 8) &&
-         g->w_out % 2 == 0 && g->w_out >= 2 && g->h_out >= 1;
+         g->w_out % 2 == 0 && g->w_out >= 32 && g->h_out >= 1;  // a warp's 32 pixels span <= 2 rows
   f.wp = g->w_out / 2;                // floor((Wo + 2 - 3) / 2) + 1 for even Wo
   f.po = (g->h_out - 1) / 2 + 1;     // floor((Ho + 2 - 3) / 2) + 1
   f.m_blocks = ceil_div(g->n * g->h_out * g->w_out, kConvBM);
   f.h_bytes = align_up(static_cast<size_t>(g->n * g->c_out * g->h_out * f.wp) * 4, 256);
-  f.e_bytes = align_up(static_cast<size_t>(f.m_blocks * g->c_out) * 4, 256);
+  const int64_t groups = ceil_div(g->n * g->h_out * g->w_out, kHmaxGroup);
+  f.e_bytes = align_up(static_cast<size_t>(groups * g->c_out) * 4, 256);
   return f;
 }
 
@@ -1009,14 +1033,19 @@ extern "C" int nplk_conv2d_maxpool_fused(void *stream, const nplk_conv_geom_t *g
   rc = f.c.mode == 8 ? launch_hmax<8>(s, f.c, wsplit, prm, fz)
                      : launch_hmax<4>(s, f.c, wsplit, prm, fz);
   if (rc) return rc;
-  const int64_t total = g->n * g->c_out * f.po * f.wp;
-  const int threads = 256;
-  const int64_t want = ceil_div(total, threads);
-  const int blocks = static_cast<int>(want < 8 * 148 * 8 ? want : 8 * 148 * 8);
-  pool_vmax_kernel<<<blocks, threads, 0, s>>>(fz.h, fz.e, out, total, static_cast<int>(g->c_out),
-                                              static_cast<int>(g->h_out),
-                                              static_cast<int>(g->w_out), fz.wp,
-                                              static_cast<int>(f.po));
+  // < 2^32: n * h_out * w_out < 2^31 (validate_conv_geom) with w_out >= 32 and c_out <= 64
+  const int64_t planes = g->n * g->c_out;
+  const bool vec = f.wp % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  const int threads = 128;
+  const int64_t items = f.po * (vec ? f.wp / 4 : f.wp);
+  const dim3 grid(static_cast<unsigned>(ceil_div(items, threads)),
+                  static_cast<unsigned>(planes < 65535 ? planes : 65535));
+  const int C = static_cast<int>(g->c_out), Ho = static_cast<int>(g->h_out),
+            Wo = static_cast<int>(g->w_out), po = static_cast<int>(f.po);
+  if (vec)
+    pool_vmax_kernel<4><<<grid, threads, 0, s>>>(fz.h, fz.e, out, planes, C, Ho, Wo, fz.wp, po);
+  else
+    pool_vmax_kernel<1><<<grid, threads, 0, s>>>(fz.h, fz.e, out, planes, C, Ho, Wo, fz.wp, po);
   count_launch();
   return launch_result();
 }

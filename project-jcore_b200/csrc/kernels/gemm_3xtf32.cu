@@ -73,6 +73,7 @@ struct GemmDst {
   float *dst[8];
   int n_dst;
   int dst_vec;  // 16-byte stores allowed into every dst
+  int rot;      // first destination this rank visits (then in turn, each warp offset by one)
   int64_t dst_col;
 };
 struct GemmNoDst {};
@@ -142,13 +143,22 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
                                                                4 * (lane & 7));
           if (row < p.M && col < p.N) {
             const int64_t off = static_cast<int64_t>(row) * p.ldc + pd.dst_col + col;
+            // Destinations in turn from a start that differs per rank and per
+            // warp, so the ranks' stores spread over all peers' links instead
+            // of all converging on the same peer at the same time.
+            int d = pd.rot + (threadIdx.x >> 5);
+            while (d >= pd.n_dst) d -= pd.n_dst;
             if (pd.dst_vec && col + 4 <= p.N) {
-              for (int d = 0; d < pd.n_dst; ++d)
+              for (int i = 0; i < pd.n_dst; ++i) {
                 *reinterpret_cast<float4 *>(pd.dst[d] + off) = val;
+                if (++d == pd.n_dst) d = 0;
+              }
             } else {
               const float e[4] = {val.x, val.y, val.z, val.w};
-              for (int d = 0; d < pd.n_dst; ++d)
+              for (int i = 0; i < pd.n_dst; ++i) {
                 for (int k = 0; k < 4 && col + k < p.N; ++k) pd.dst[d][off + k] = e[k];
+                if (++d == pd.n_dst) d = 0;
+              }
             }
           }
         }
@@ -832,6 +842,9 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
   GemmDst pd{};
   pd.n_dst = n_dst;
   pd.dst_col = col_offset;
+  // This rank's index when the blocks are laid out by rank (col_offset =
+  // rank * N_local, dst[] in rank order): it starts with the next rank.
+  pd.rot = static_cast<int>((col_offset / N_local + 1) % n_dst);
   bool vec = N_local % 4 == 0 && ldc % 4 == 0 && col_offset % 4 == 0;
   for (int d = 0; d < n_dst; ++d) {
     if (!dst[d]) return kErrInvalidArg;
