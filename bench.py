@@ -337,6 +337,33 @@ def _reference_cpu_timed(ref_lib, steps, warmup, rows=False):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+def bind_host_to_gpu(local_rank):
+    """Restricts this process to the CPUs NVML reports as local to its GPU, so
+    the e2e leg's pinned host buffers live on, and are copied from, the GPU's
+    own socket. Returns the number of CPUs bound, or None when NVML or the
+    affinity call is unavailable (the process is then left as it was)."""
+    try:
+        import pynvml
+        import torch
+        pr = torch.cuda.get_device_properties(local_rank)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            ncpu = os.cpu_count() or 1
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (ncpu + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {i * 64 + b for i, word in enumerate(words) for b in range(64)
+                if (int(word) >> b) & 1 and i * 64 + b < ncpu}
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+        return len(cpus)
+    except Exception:  # no NVML, no affinity support: leave the process as it is
+        return None
+
+
 def run_b200(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -426,6 +453,9 @@ def run_b200(args, rank, world, local_rank):
     ms_per_step, conv_kernel_ms = stats.tolist()
 
     # ---- e2e through the public C ABI with pinned host buffers ----
+    # With several ranks, each process first moves to its GPU's local CPUs so
+    # its pinned buffers sit on that socket.
+    cpus_bound = bind_host_to_gpu(local_rank) if world > 1 else None
     hx = torch.from_numpy(x).pin_memory()
     hw_ = torch.from_numpy(w).pin_memory()
     hy = torch.empty((N_IMG, C_OUT, HW_IN, HW_IN)).pin_memory()
@@ -460,6 +490,26 @@ def run_b200(args, rank, world, local_rank):
     # ---- parity spot check of the timed output (device result vs host API result) ----
     torch.cuda.synchronize()
     same = torch.allclose(ty.cpu(), hy, rtol=0, atol=0)
+    # The host link alone: the same bytes copied host->device and back from
+    # the same pinned buffers, all ranks at once, no kernels.
+    dx, dy = torch.empty_like(tx), torch.empty_like(ty)
+    for _ in range(2):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(dy, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dx.copy_(hx, non_blocking=True)
+        hy.copy_(dy, non_blocking=True)
+        torch.cuda.synchronize()
+    link_s = torch.tensor([(time.perf_counter() - t0) / args.steps], device=dev,
+                          dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(link_s, op=dist.ReduceOp.MAX)
+    link_step = float(link_s.item())
+    del dx, dy
 
     result = None
     if rank == 0:
@@ -499,6 +549,14 @@ def run_b200(args, rank, world, local_rank):
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "api": "npl_conv2d_bn_activation on pinned host tensors (library stages)",
+                "host_link": {
+                    "copy_ms_per_step": round(link_step * 1e3, 4),
+                    "GB/s_per_rank": round((hx.numel() + hy.numel()) * 4 / link_step / 1e9, 2),
+                    "what": "the step's input and output bytes copied host->device and back "
+                            "from the same pinned buffers, no kernels, all ranks at once "
+                            "(max over ranks)",
+                    "cpus_bound_per_rank": cpus_bound,
+                },
             },
             "roofline": {
                 "bound": "tensor",
