@@ -16,6 +16,8 @@ and checks the kernel status word.
     python -m npl_b200.profile_cases bandwidth # BN, ReLU, GAP on 256x512x14x14; softmax 102400x1000
     python -m npl_b200.profile_cases allgather # fused GEMM all-gather epilogue, 2 simulated ranks
     python -m npl_b200.profile_cases conv_pair # the 3x3 conv on CTA pairs
+    python -m npl_b200.profile_cases conv_n256 # the 3x3 conv at N=256 (output beyond L2)
+    python -m npl_b200.profile_cases stem_fused # stem conv + pool, and the fused form (N=16)
 
 Run from the package directory (``project-jcore_b200``) or with it on sys.path.
 """
@@ -171,6 +173,37 @@ def case_allgather(reps: int = 2, m: int = 4096, n_local: int = 2048, k: int = 4
     assert lib.nplk_read_status(s) == 0
 
 
+def case_stem_fused(reps: int = 2, n: int = 16):
+    """The stem block both ways: conv (+BN+ReLU) then 3x3/s2 max pool, and the
+    fused nplk_conv2d_maxpool_fused, `reps` rounds."""
+    from . import conv_geom
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    g = conv_geom(n, 3, 224, 224, 64, 7, 7, 2, 3)
+    x = torch.rand(n, 3, 224, 224, device="cuda", generator=gen) * 2 - 1
+    w = torch.randn(64, 3, 7, 7, device="cuda", generator=gen) * (2.0 / 147) ** 0.5
+    bn = [torch.rand(64, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    y = torch.empty(n, 64, 112, 112, device="cuda")
+    pooled = torch.empty(n, 64, 56, 56, device="cuda")
+    fused = torch.empty_like(pooled)
+    ws = lib.nplk_conv_workspace_size(C.byref(g))
+    work = torch.empty(ws // 4 + 64, device="cuda")
+    fws = lib.nplk_conv2d_maxpool_workspace_size(C.byref(g))
+    fwork = torch.empty(fws // 4 + 64, device="cuda")
+    for _ in range(reps):
+        assert lib.nplk_conv2d_fused(s, C.byref(g), _p(x), _p(w), None, _p(bn[0]), _p(bn[1]),
+                                     _p(bn[2]), _p(bn[3]), 1e-5, 1, 0.0, _p(y), _p(work), ws,
+                                     None) == 0
+        assert lib.nplk_pool2d(s, n, 64, 112, 112, 3, 3, 2, 2, 1, 1, 56, 56, 0, 0, _p(y),
+                               _p(pooled)) == 0
+        assert lib.nplk_conv2d_maxpool_fused(s, C.byref(g), _p(x), _p(w), None, _p(bn[0]),
+                                             _p(bn[1]), _p(bn[2]), _p(bn[3]), 1e-5, 1, 0.0,
+                                             _p(fused), _p(fwork), fws, None) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
+    assert torch.equal(fused, pooled)
+
+
 CASES = {"conv": case_conv,
          "conv_direct": lambda: case_conv(algo=1),
          "conv_window_tma": lambda: case_conv(algo=3),
@@ -180,7 +213,9 @@ CASES = {"conv": case_conv,
          "gemm_raw": lambda: case_gemm(raw=True),
          "gemm_1024": lambda: case_gemm(m=1024, n=1024, k=1024),
          "bandwidth": case_bandwidth, "allgather": case_allgather,
-         "conv_pair": lambda: case_conv(algo=5)}
+         "conv_pair": lambda: case_conv(algo=5),
+         "conv_n256": lambda: case_conv(n=256),
+         "stem_fused": case_stem_fused}
 
 if __name__ == "__main__":
     name = sys.argv[1] if len(sys.argv) > 1 else "conv"
