@@ -379,9 +379,13 @@ NPL_API int nplk_conv2d_tune(void *stream, const nplk_conv_geom_t *g, const floa
                              float bn_eps, int act, float act_alpha, float *out,
                              void *workspace, size_t workspace_bytes, int reps, int *best_algo,
                              float *best_us);
-/* The same for the GEMM's tile width: C = A @ B (alpha 1, beta 0) with BN 64
- * and 128, `reps` timed runs each; caches and returns the faster BN. The
- * workspace is the split form's (nplk_gemm_workspace_size). */
+/* The same for the GEMM's tile configuration: C = A @ B (alpha 1, beta 0)
+ * with 64-wide tiles, 128-wide tiles, and (K >= 512) 128-wide tiles with K
+ * cut in two slices added into a zeroed C; `reps` timed runs each; caches and
+ * returns the fastest as 64, 128 or 1128. nplk_gemm uses two K slices only
+ * for a plain product (beta 0, no bias, no activation) in the split operand
+ * form; otherwise a cached 1128 means 128-wide tiles. The workspace is the
+ * split form's (nplk_gemm_workspace_size). */
 NPL_API int nplk_gemm_tune(void *stream, int64_t M, int64_t N, int64_t K, const float *A,
                            int64_t lda, const float *B, int64_t ldb, float *C, int64_t ldc,
                            void *workspace, size_t workspace_bytes, int reps, int *best_bn,

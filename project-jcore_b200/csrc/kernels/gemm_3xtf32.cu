@@ -60,10 +60,21 @@ struct GemmParams {
   const float *bias;
   int act;
   float act_alpha;
-  int one_pass;
+  int one_pass;       // bit 0: one TF32 pass; bits 8..15: K slices per tile (gemm_k_slices)
   uint32_t stall_us;  // fault injection: 0 except on an armed launch (injected_stall)
   int *status;
 };
+
+__device__ __forceinline__ bool gemm_one_pass(const GemmParams &p) { return (p.one_pass & 1) != 0; }
+
+// Split-K: each tile's K range is cut into this many slices, each a separate
+// work unit whose epilogue adds alpha * (its partial product) into C, which
+// the host zeroed (beta 0, no bias, no activation). Two slices added to zero
+// give the same sum in either order, so the result stays deterministic.
+__device__ __forceinline__ int gemm_k_slices(const GemmParams &p) {
+  const int s = (p.one_pass >> 8) & 255;
+  return s > 1 ? s : 1;
+}
 
 // nplk_gemm_allgather: every output is stored to each of dst[0..n_dst) at
 // column dst_col + col (row pitch GemmParams::ldc). A kernel parameter of the
@@ -100,9 +111,21 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
                                                    float *stg) {
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
+    const int col0 = nb * BN + c0;
+    // The row's C values for beta, loaded before the accumulator is read so
+    // that their latency overlaps the TMEM load, and all eight in flight at
+    // once (loads placed after a store to C would each wait for it).
+    const bool vec_chunk = !kFused && vec_ok && r < p.M && col0 + 32 <= p.N;
+    float4 cv[8];
+    if (vec_chunk && p.beta != 0.0f) {
+      const float4 *src = reinterpret_cast<const float4 *>(p.C + static_cast<int64_t>(r) * p.ldc +
+                                                           col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cv[q] = src[q];
+    }
     uint32_t v[32], w[32];
     tmem_ld32(t_row + c0, v);
-    if (!p.one_pass) {
+    if (!gemm_one_pass(p)) {
       tmem_ld32(t_row + BN + c0, w);
       tmem_wait_ld2(v, w);
     } else {
@@ -110,7 +133,6 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
 #pragma unroll
       for (int j = 0; j < 32; ++j) w[j] = 0u;
     }
-    const int col0 = nb * BN + c0;
     if constexpr (kFused) {
       // Fused exchange: bias and activation, then the same values to every
       // destination buffer (this GPU's and the peers' over NVLink). The warp's
@@ -170,30 +192,41 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         out[j] = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
-      if (vec_ok && col0 + 32 <= p.N) {
+      if (gemm_k_slices(p) > 1) {
+        // a K slice's partial product, added into the zeroed C
+        if (vec_ok && col0 + 32 <= p.N) {
+          float4 *dst = reinterpret_cast<float4 *>(crow + col0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            atomicAdd(dst + q, make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2],
+                                           out[4 * q + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) atomicAdd(crow + col0 + j, out[j]);
+        }
+      } else if (vec_chunk) {
+        // every load (C, bias) before the first store
+        if (p.beta != 0.0f) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            out[4 * q] += p.beta * cv[q].x;
+            out[4 * q + 1] += p.beta * cv[q].y;
+            out[4 * q + 2] += p.beta * cv[q].z;
+            out[4 * q + 3] += p.beta * cv[q].w;
+          }
+        }
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) out[j] += p.bias[col0 + j];
+        }
         float4 *dst = reinterpret_cast<float4 *>(crow + col0);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 o = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
-          if (p.beta != 0.0f) {
-            const float4 c = dst[q];
-            o.x += p.beta * c.x;
-            o.y += p.beta * c.y;
-            o.z += p.beta * c.z;
-            o.w += p.beta * c.w;
-          }
-          if (p.bias) {
-            o.x += p.bias[col0 + 4 * q];
-            o.y += p.bias[col0 + 4 * q + 1];
-            o.z += p.bias[col0 + 4 * q + 2];
-            o.w += p.bias[col0 + 4 * q + 3];
-          }
-          o.x = apply_act(o.x, p.act, p.act_alpha);
-          o.y = apply_act(o.y, p.act, p.act_alpha);
-          o.z = apply_act(o.z, p.act, p.act_alpha);
-          o.w = apply_act(o.w, p.act, p.act_alpha);
-          dst[q] = o;
-        }
+        for (int q = 0; q < 8; ++q)
+          dst[q] = make_float4(apply_act(out[4 * q], p.act, p.act_alpha),
+                               apply_act(out[4 * q + 1], p.act, p.act_alpha),
+                               apply_act(out[4 * q + 2], p.act, p.act_alpha),
+                               apply_act(out[4 * q + 3], p.act, p.act_alpha));
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -258,6 +291,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_tiles = p.m_blocks * p.n_blocks;
+  // Work unit u: tile u / KS, K slice u % KS (k-blocks [ks * kbp, (ks + 1) * kbp)).
+  const int KS = gemm_k_slices(p);
+  const int kbp = (p.k_blocks + KS - 1) / KS;
+  const int num_units = num_tiles * KS;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -267,10 +304,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t pending = 0;  // stages that received a copy, with its phase
       uint32_t pending_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+        const int tile = unit / KS;
+        const int kb0 = (unit - tile * KS) * kbp;
+        const int kb1 = kb0 + kbp < p.k_blocks ? kb0 + kbp : p.k_blocks;
         int mb, nb;
         gemm_tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.status,
                          kStatusTimeoutProducer))
             goto producer_done;
@@ -304,7 +344,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       const bool go = injected_stall(never, p.stall_us, abort_flag, p.status);
-      for (int tile = blockIdx.x; go && tile < num_tiles; tile += gridDim.x, ++local) {
+      for (int unit = blockIdx.x; go && unit < num_units; unit += gridDim.x, ++local) {
+        const int tile = unit / KS;
+        const int kb0 = (unit - tile * KS) * kbp;
+        const int kb1 = kb0 + kbp < p.k_blocks ? kb0 + kbp : p.k_blocks;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, abort_flag, p.status,
@@ -312,7 +355,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         tc_fence_after_sync();
         const uint32_t d_tmem = tmem_base + acc * T::kAccCols;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutMma))
             goto mma_done;
           tc_fence_after_sync();
@@ -321,16 +364,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t a_desc = a_desc0 + static_cast<uint64_t>(stage * (T::kAStageBytes >> 4));
           const uint64_t b_desc = b_desc0 + static_cast<uint64_t>(stage * (T::kBStageBytes >> 4));
           constexpr uint64_t kLoOff = (kGemmBM * 128) >> 4;
-          if (p.one_pass) {
+          if (gemm_one_pass(p)) {
 #pragma unroll
             for (int kk = 0; kk < kGemmBK / 8; ++kk)
               mma_tf32_ss(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc_n,
-                          (kb > 0 || kk > 0) ? 1u : 0u);
+                          (kb > kb0 || kk > 0) ? 1u : 0u);
           } else {
 #pragma unroll
             for (int kk = 0; kk < kGemmBK / 8; ++kk) {
               mma_tf32_ss(d_tmem, a_desc + 2 * kk, b_desc + 2 * kk, idesc_2n,
-                          (kb > 0 || kk > 0) ? 1u : 0u);
+                          (kb > kb0 || kk > 0) ? 1u : 0u);
               mma_tf32_ss(d_tmem, a_desc + kLoOff + 2 * kk, b_desc + 2 * kk, idesc_n, 1u);
             }
           }
@@ -354,7 +397,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
                         ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
     int local = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
+      const int tile = unit / KS;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
@@ -529,7 +573,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
           const uint64_t a_raw = umma_desc_sw128(st);
           const uint64_t a_lo = umma_desc_sw128(st + T::kAHalf);
           const uint64_t b = umma_desc_mn_sw128_32b(st + 2 * T::kAHalf, T::kBAtom);
-          if (p.one_pass) {
+          if (gemm_one_pass(p)) {
 #pragma unroll
             for (int kk = 0; kk < kGemmBK / 8; ++kk)
               mma_tf32_ss(d_tmem, a_raw + 2 * kk, b + 64 * kk, idesc_n,
@@ -589,7 +633,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
     for (int it = 0; it < items; ++it) {
       if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kStatusTimeoutStage)) break;
       uint8_t *st = smem + stage * T::kStageBytes;
-      if (!p.one_pass) {
+      if (!gemm_one_pass(p)) {
         const float4 *a4 = reinterpret_cast<const float4 *>(st);
         float4 *al4 = reinterpret_cast<float4 *>(st + T::kAHalf);
 #pragma unroll 4
@@ -631,25 +675,38 @@ namespace {
 
 struct GemmPlan {
   int bn;
+  int ks;  // K slices per tile (split-K; only for calls gemm_run finds eligible)
   int64_t m_blocks, n_blocks, kp;
   size_t a_bytes, b_bytes;
   size_t b_bytes_max;  // B' for either tile width (the workspace size covers both)
 };
 
-// Output-tile width: force_bn when 64 or 128, else the tile-configuration
-// cache's entry for the shape, else 128 when the 128-wide tiles fill the SMs.
-GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int force_bn = 0) {
+// Tile configurations as the tile-configuration cache stores them: the tile
+// width BN, plus 1000 per extra K slice (1128 = 128 wide, K in two slices).
+constexpr int kGemmCfgSplitK = 1128;
+bool valid_gemm_cfg(int c) { return c == 64 || c == 128 || c == kGemmCfgSplitK; }
+
+// Configuration: force_cfg when valid, else the tile-configuration cache's
+// entry for the shape, else 128-wide tiles when they fill the SMs, else, when
+// two K slices of 128-wide tiles still fit on the SMs and K has at least 16
+// k-blocks, those (split-K), else 64-wide tiles.
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int force_cfg = 0) {
   GemmPlan g{};
   g.m_blocks = ceil_div(M, kGemmBM);
   g.kp = ceil_div(K, kGemmBK) * kGemmBK;
   const int64_t tiles128 = g.m_blocks * ceil_div(N, 128);
-  g.bn = (tiles128 >= sm_count()) ? 128 : 64;
+  int cfg = tiles128 >= sm_count() ? 128
+            : (2 * tiles128 <= sm_count() && g.kp / kGemmBK >= 16) ? kGemmCfgSplitK
+                                                                  : 64;
   int cached = 0;
-  if (force_bn == 64 || force_bn == 128)
-    g.bn = force_bn;
+  if (valid_gemm_cfg(force_cfg))
+    cfg = force_cfg;
   else if (!tuning_cache_empty() && tuning_lookup(tuning_key_gemm(M, N, K), &cached) &&
-           (cached == 64 || cached == 128))
-    g.bn = cached;
+           valid_gemm_cfg(cached))
+    cfg = cached;
+  g.bn = cfg % 1000;
+  g.ks = cfg / 1000 + 1;
+  if (g.ks > 1 && g.kp / kGemmBK < 2 * g.ks) g.ks = 1;  // every slice keeps >= 2 k-blocks
   g.n_blocks = ceil_div(N, g.bn);
   g.a_bytes = align_up(static_cast<size_t>(g.m_blocks) * 2 * kGemmBM * g.kp * 4, 256);
   g.b_bytes = align_up(static_cast<size_t>(g.n_blocks) * 2 * g.bn * g.kp * 4, 256);
@@ -668,7 +725,7 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
   rc = encode_tmap_2d_f32_sw128(&map_b, b_split, g.kp, g.n_blocks * 2 * BN, g.kp * 4, kGemmBK,
                                 2 * BN);
   if (rc) return rc;
-  const int64_t tiles = g.m_blocks * g.n_blocks;
+  const int64_t tiles = g.m_blocks * g.n_blocks * g.ks;  // work units
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
   // The epilogue staging block only for the fused exchange: with programmatic
   // dependent launch the GEMM's CTAs become resident while the split kernels
@@ -726,13 +783,13 @@ int launch_gemm_raw(cudaStream_t stream, const GemmPlan &g, const float *A, int6
 
 }  // namespace
 
-// Split launchers (split_tf32.cu).
-int launch_split_rows(cudaStream_t s, const float *src, int64_t rows, int64_t cols, int64_t ld,
-                      int64_t col_offset, float *dst, int row_block, int64_t kp,
-                      int64_t rows_pad);
-int launch_split_transpose(cudaStream_t s, const float *src, int64_t krows, int64_t ncols,
-                           int64_t ld, float *dst, int row_block, int64_t kp, int64_t npad,
-                           bool overlap_previous = false);
+// Split launcher (split_tf32.cu): A -> A' and B -> B' (hi/lo, blocked,
+// zero-padded), and C zeroed when `c` is non-null, in one launch.
+int launch_split_operands(cudaStream_t s, const float *a, int64_t rows, int64_t cols,
+                          int64_t lda, float *a_dst, int a_row_block, int64_t rows_pad,
+                          const float *b, int64_t krows, int64_t ncols, int64_t ldb,
+                          float *b_dst, int b_row_block, int64_t npad, int64_t kp, float *c,
+                          int64_t ldc);
 
 }  // namespace nplk
 
@@ -757,7 +814,13 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   if (lda < K || ldb < N) return kErrInvalidArg;
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
     return kErrUnsupported;
-  const GemmPlan g = plan_gemm(M, N, K, force_bn);
+  GemmPlan g = plan_gemm(M, N, K, force_bn);
+  // Split-K only where its epilogue applies: a plain product written to C
+  // (no C read, bias, activation or fused exchange) in the split operand form.
+  if (g.ks > 1 && (pd || prm.beta != 0.0f || prm.bias || prm.act != 0 ||
+                   (flags & NPLK_GEMM_RAW_OPERANDS) || !workspace ||
+                   workspace_bytes < g.a_bytes + g.b_bytes))
+    g = plan_gemm(M, N, K, g.bn);
   if (!status) status = device_status_word();
   if (!status) return kErrInternal;
   prm.M = static_cast<int>(M);
@@ -766,7 +829,7 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   prm.m_blocks = static_cast<int>(g.m_blocks);
   prm.n_blocks = static_cast<int>(g.n_blocks);
   prm.k_blocks = static_cast<int>(g.kp / kGemmBK);
-  prm.one_pass = (flags & NPLK_GEMM_TF32_FAST) ? 1 : 0;
+  prm.one_pass = ((flags & NPLK_GEMM_TF32_FAST) ? 1 : 0) | (g.ks > 1 ? g.ks << 8 : 0);
   prm.stall_us = take_armed_stall(NPLK_DEBUG_GEMM);
   prm.status = status;
 
@@ -791,12 +854,12 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   float *a_split = static_cast<float *>(workspace);
   float *b_split = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + g.a_bytes);
 
-  int rc = launch_split_rows(s, A, M, K, lda, 0, a_split, kGemmBM, g.kp, g.m_blocks * kGemmBM);
-  if (rc) return rc;
-  // The B split overlaps the A split and the GEMM kernel's set-up overlaps
-  // both (programmatic dependent launch); the GEMM's TMA producer waits for
-  // the splits before its first load.
-  rc = launch_split_transpose(s, B, K, N, ldb, b_split, g.bn, g.kp, g.n_blocks * g.bn, true);
+  // One launch splits A and B (and zeroes C for the K slices to add into);
+  // the GEMM kernel's set-up overlaps it (programmatic dependent launch) and
+  // its TMA producer waits for it before the first load.
+  const int rc = launch_split_operands(s, A, M, K, lda, a_split, kGemmBM, g.m_blocks * kGemmBM,
+                                       B, K, N, ldb, b_split, g.bn, g.n_blocks * g.bn, g.kp,
+                                       g.ks > 1 ? prm.C : nullptr, prm.ldc);
   if (rc) return rc;
   if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm, pd);
   return launch_gemm<64>(s, g, a_split, b_split, prm, pd);
@@ -875,7 +938,8 @@ extern "C" int nplk_gemm_tune(void *stream, int64_t M, int64_t N, int64_t K, con
   }
   int best = 0, rc = kOk;
   float best_ms = 0.0f;
-  for (int bn : {64, 128}) {
+  for (int bn : {64, 128, kGemmCfgSplitK}) {
+    if (bn == kGemmCfgSplitK && ceil_div(K, kGemmBK) < 16) continue;
     std::vector<float> ms;
     for (int r = 0; r <= reps && rc == kOk; ++r) {
       if (cudaEventRecord(e0, s) != cudaSuccess) rc = kErrInternal;

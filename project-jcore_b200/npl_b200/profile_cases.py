@@ -212,6 +212,7 @@ CASES = {"conv": case_conv,
          "layernorm": case_layernorm, "pool": case_pool,
          "gemm_raw": lambda: case_gemm(raw=True),
          "gemm_1024": lambda: case_gemm(m=1024, n=1024, k=1024),
+         "gemm_raw_1024": lambda: case_gemm(m=1024, n=1024, k=1024, raw=True),
          "bandwidth": case_bandwidth, "allgather": case_allgather,
          "conv_pair": lambda: case_conv(algo=5),
          "conv_n256": lambda: case_conv(n=256),

@@ -224,3 +224,31 @@ def test_gemm_infinity_and_raw_eligibility(form):
     rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 1.0, S.dptr(A2), k + 1, S.dptr(B), n, 0.0,
                        S.dptr(Cm), n, None, 0, 0.0, nb.NPLK_GEMM_RAW_OPERANDS, None, 0, None)
     assert rc == nb.NPL_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("m,n,k", [(1024, 1024, 1024), (300, 260, 520), (128, 1000, 4096),
+                                   (1000, 96, 2048)])
+def test_gemm_split_k_plain_products(m, n, k):
+    # Small products whose 128-wide tiles fill at most half the SMs run with K
+    # cut in two slices added into a zeroed C (beta 0, no bias, no activation):
+    # checked against fp64, deterministic from call to call, and with a
+    # pre-filled C (beta 0 must not read it).
+    import torch
+    lib = S.gpu_lib()
+    gen = torch.Generator(device="cuda").manual_seed(m + 7 * n + k)
+    A = torch.rand(m, k, device="cuda", generator=gen) * 2 - 1
+    B = torch.rand(k, n, device="cuda", generator=gen) * 2 - 1
+    ws = lib.nplk_gemm_workspace_size(m, n, k)
+    work = torch.empty(ws // 4 + 64, device="cuda")
+    outs = []
+    for fill in (float("nan"), 3.0):
+        Cm = torch.full((m, n), fill, device="cuda")
+        rc = lib.nplk_gemm(S.cuda_stream(), m, n, k, 0.5, S.dptr(A), k, S.dptr(B), n, 0.0,
+                           S.dptr(Cm), n, None, 0, 0.0, 0, S.dptr(work), ws, None)
+        assert rc == 0
+        torch.cuda.synchronize()
+        outs.append(Cm.clone())
+    assert lib.nplk_read_status(S.cuda_stream()) == 0
+    assert torch.equal(outs[0], outs[1])
+    ref = 0.5 * (A.double() @ B.double())
+    assert ((outs[0].double() - ref).abs().max() / ref.abs().max()).item() < TOL
