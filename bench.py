@@ -1051,11 +1051,15 @@ def gemm_dist(args, rank, world, local_rank):
     # C over NVLink (CUDA IPC peer pointers); C is complete on every rank when
     # all ranks' kernels have finished, i.e. after the max over ranks of the
     # per-rank device time.
+    # The peers are written through the TMA unit (the default) and, for
+    # comparison, by 16-byte stores from the epilogue threads; C is checked
+    # after the TMA form, which runs last.
     full_f = torch.empty(GEMM_M, GEMM_N, device=dev)
     peers = nd.PeerBuffers(full_f, world, rank)
-    try:
+
+    def fused_ms(flags):
         for _ in range(2):
-            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work)
+            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work, flags=flags)
         torch.cuda.synchronize()
         dist.barrier()
         f_ms = []
@@ -1063,17 +1067,21 @@ def gemm_dist(args, rank, world, local_rank):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work)
+            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work, flags=flags)
             e1.record(stream)
             torch.cuda.synchronize()
             dist.barrier()
             f_ms.append(e0.elapsed_time(e1))
         tf = torch.tensor([statistics.mean(f_ms)], device=dev, dtype=torch.float64)
         dist.all_reduce(tf, op=dist.ReduceOp.MAX)
+        return tf.item()
+
+    try:
+        sm_ms = fused_ms(nb.NPLK_GEMM_PEER_SM_STORES)
+        fm = fused_ms(0)
         ferr = ((full_f[rows].double() - ref).abs().max() / ref.abs().max()).item()
     finally:
         peers.close()
-    fm = tf.item()
     # Every rank's whole C against a one-GPU GEMM of the same inputs on this
     # rank (same k order and epilogue, so bit-identical is expected), for
     # both exchange forms.
@@ -1112,8 +1120,13 @@ def gemm_dist(args, rank, world, local_rank):
                       "c_max_normwise_diff_all_ranks": float(diff.item()),
                       "peer_egress_bytes_per_rank": egress,
                       "peer_egress_GB/s_per_rank": round(egress / (fm / 1e3) / 1e9, 1),
-                      "step": "nplk_gemm_allgather: the GEMM epilogue stores every tile into "
-                              "all ranks' C over NVLink (CUDA IPC peer pointers)"},
+                      "step": "nplk_gemm_allgather: the GEMM epilogue hands every 32x32 piece "
+                              "to the TMA unit, which stores it into all ranks' C over NVLink "
+                              "(CUDA IPC peer pointers)",
+                      "thread_stores": {"ms": round(sm_ms, 4),
+                                        "value": round(GEMM_FLOPS / (sm_ms / 1e3) / 1e12, 2),
+                                        "step": "the same with 16-byte stores from the epilogue "
+                                                "threads (NPLK_GEMM_PEER_SM_STORES)"}},
             "normwise_err_sampled_rows": err}
 
 

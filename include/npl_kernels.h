@@ -57,6 +57,11 @@ extern "C" {
  * do not qualify). */
 #define NPLK_GEMM_SPLIT_OPERANDS 2u
 #define NPLK_GEMM_RAW_OPERANDS 4u
+/* nplk_gemm_allgather: store into the destinations from the epilogue threads
+ * (16-byte stores) instead of through the TMA unit (the default whenever the
+ * destinations are 16-byte aligned with ldc and col_offset multiples of 4 and
+ * the split operand form runs). Both give the same C. */
+#define NPLK_GEMM_PEER_SM_STORES 8u
 
 /* ---- dense contractions (tcgen05, 3xTF32) ---------------------------------- */
 
@@ -305,7 +310,10 @@ NPL_API int nplk_ipc_close_handle(void *dev_ptr, uint64_t offset);
  * usual layout (dst[] in rank order, col_offset = rank * N_local) each rank
  * visits the destinations starting after its own index, so the ranks' stores
  * spread over all peers instead of converging on one; any order gives the
- * same C. beta is 0 (C is not read); other arguments as nplk_gemm. */
+ * same C. The epilogue hands each 32 x 32 piece to the TMA unit once per
+ * destination (NPLK_GEMM_PEER_SM_STORES: 16-byte stores from the epilogue
+ * threads instead), so the NVLink writes drain while the next piece is formed.
+ * beta is 0 (C is not read); other arguments as nplk_gemm. */
 NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
                                 float alpha, const float *A, int64_t lda, const float *B,
                                 int64_t ldb, const float *bias, int act, float act_alpha,

@@ -22,6 +22,7 @@
 #include <math_constants.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <vector>
 
 #include "nplk_device.cuh"
@@ -49,6 +50,9 @@ struct GemmTraits {
   static constexpr int kTmemCols = 2 * kAccCols;  // two accumulators
   static constexpr int kBarrierBytes = 256;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + kEpiStageBytes;
+  // The TMA-store exchange: barriers in a 1 KB slot, then the 1024-byte
+  // aligned staging boxes (4 epilogue warps x 2 boxes x 4 KB).
+  static constexpr int kSmemBytesTma = 1024 + kStages * kStageBytes + 1024 + 32768;
 };
 
 struct GemmParams {
@@ -89,6 +93,18 @@ struct GemmDst {
 };
 struct GemmNoDst {};
 
+// nplk_gemm_allgather, TMA-store form: map[d] is destination d's block of
+// columns [dst_col, dst_col + N_local) as a [M][N_local] fp32 tensor (row pitch
+// ldc, 32 x 32 boxes, 128-byte swizzle). Each epilogue warp stages its 32 x 32
+// piece of the accumulator in shared memory and one lane hands it to the TMA
+// unit once per destination, so the NVLink writes drain asynchronously while
+// the warp goes on to the next piece (two staging boxes per warp).
+struct alignas(64) GemmDstTma {
+  CUtensorMap map[8];
+  int n_dst;
+  int rot;
+};
+
 // Tile order: groups of 8 M-blocks sweep all N-blocks, so the CTAs resident at
 // one time share A row-blocks and B column-blocks in L2.
 __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_blocks, int &mb,
@@ -108,7 +124,7 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int m_blocks, int n_b
 template <int BN, bool kFused, class Dst>
 __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Dst &pd,
                                                    uint32_t t_row, int r, int nb, bool vec_ok,
-                                                   float *stg) {
+                                                   float *stg, int &box_seq) {
 #pragma unroll 1
   for (int c0 = 0; c0 < BN; c0 += 32) {
     const int col0 = nb * BN + c0;
@@ -133,7 +149,43 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
 #pragma unroll
       for (int j = 0; j < 32; ++j) w[j] = 0u;
     }
-    if constexpr (kFused) {
+    if constexpr (std::is_same<Dst, GemmDstTma>::value) {
+      // Fused exchange through the TMA unit: bias and activation, the warp's
+      // 32 x 32 piece into a staging box (rows of 128 bytes, 16-byte chunk j
+      // of row i at chunk j ^ (i mod 8): the map's 128-byte swizzle, and
+      // conflict-free for each quarter-warp's stores), then one tensor store
+      // per destination. Rows and columns past the block are clipped by TMA.
+      const int lane = threadIdx.x & 31;
+      if (col0 < p.N) {
+        float *box = stg + (box_seq & 1) * 1024;
+        if (lane == 0) bulk_wait_group_read<1>();  // this box's previous stores have read it
+        __syncwarp();
+        float out[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float o = p.alpha * (__uint_as_float(v[j]) + __uint_as_float(w[j]));
+          if (p.bias && col0 + j < p.N) o += p.bias[col0 + j];
+          out[j] = apply_act(o, p.act, p.act_alpha);
+        }
+        uint8_t *row = reinterpret_cast<uint8_t *>(box) + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4 *>(row + ((q ^ (lane & 7)) << 4)) =
+              make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          int d = pd.rot + (threadIdx.x >> 5);
+          while (d >= pd.n_dst) d -= pd.n_dst;
+          for (int i = 0; i < pd.n_dst; ++i) {
+            tma_store_2d(&pd.map[d], box, col0, r - lane);
+            if (++d == pd.n_dst) d = 0;
+          }
+          bulk_commit_group();
+        }
+        ++box_seq;
+      }
+    } else if constexpr (kFused) {
       // Fused exchange: bias and activation, then the same values to every
       // destination buffer (this GPU's and the peers' over NVLink). The warp's
       // 32 x 32 block goes through shared memory so that each store
@@ -391,12 +443,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = quad * 32 + lane;
-    float *stg = reinterpret_cast<float *>(smem_b + T::kStages * T::kBStageBytes +
-                                           T::kBarrierBytes) +
-                 (warp - 2) * 32 * kEpiStagePitch;
+    constexpr bool kTmaDst = std::is_same<Dst, GemmDstTma>::value;
+    float *stg = kTmaDst ? reinterpret_cast<float *>(smem_b + T::kStages * T::kBStageBytes + 1024) +
+                               (warp - 2) * 2 * 1024
+                         : reinterpret_cast<float *>(smem_b + T::kStages * T::kBStageBytes +
+                                                     T::kBarrierBytes) +
+                               (warp - 2) * 32 * kEpiStagePitch;
     const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
                         ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
     int local = 0;
+    int box_seq = 0;
     for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x, ++local) {
       const int tile = unit / KS;
       const int acc = local & 1;
@@ -409,11 +465,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int r = mb * kGemmBM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
-gemm_epilogue_tile<BN, kFused>(p, pd, t_row, r, nb, vec_ok, stg);
+      gemm_epilogue_tile<BN, kFused>(p, pd, t_row, r, nb, vec_ok, stg, box_seq);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
+    // Every tensor store of this warp complete before the CTA exits.
+    if (kTmaDst && lane == 0) bulk_wait_group<0>();
   }
 
   __syncthreads();
@@ -605,6 +663,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
     const bool vec_ok = (p.N % 4 == 0) && (p.ldc % 4 == 0) &&
                         ((reinterpret_cast<uintptr_t>(p.C) & 15u) == 0);
     int local = 0;
+    int box_seq = 0;  // (TMA-store boxes; unused by this form)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -616,7 +675,7 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(acc * T::kAccCols);
       gemm_epilogue_tile<BN, kFused>(p, pd, t_row, mb * kGemmBM + row_in_tile, nb, vec_ok,
-                                     stg);
+                                     stg, box_seq);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -716,7 +775,8 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int force_cfg = 0) {
 
 template <int BN>
 int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
-                const float *b_split, const GemmParams &prm, const GemmDst *pd) {
+                const float *b_split, const GemmParams &prm, const GemmDst *pd,
+                const GemmDstTma *pt) {
   using T = GemmTraits<BN>;
   CUtensorMap map_a, map_b;
   int rc = encode_tmap_2d_f32_sw128(&map_a, a_split, g.kp, g.m_blocks * 2 * kGemmBM, g.kp * 4,
@@ -730,6 +790,13 @@ int launch_gemm(cudaStream_t stream, const GemmPlan &g, const float *a_split,
   // The epilogue staging block only for the fused exchange: with programmatic
   // dependent launch the GEMM's CTAs become resident while the split kernels
   // still run, and 18 KB less shared memory leaves those room on the SM.
+  if (pt) {
+    auto *fn = gemm_3xtf32_kernel<BN, true, GemmDstTma>;
+    rc = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), T::kSmemBytesTma);
+    if (rc) return rc;
+    return launch_programmatic(fn, dim3(grid), dim3(kGemmThreads), T::kSmemBytesTma, stream,
+                               map_a, map_b, prm, *pt);
+  }
   if (pd) {
     auto *fn = gemm_3xtf32_kernel<BN, true, GemmDst>;
     rc = ensure_dynamic_smem(reinterpret_cast<const void *>(fn), T::kSmemBytes);
@@ -809,7 +876,8 @@ namespace {
 // select; `pd` non-null selects the fused exchange epilogue.
 int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, int64_t lda,
              const float *B, int64_t ldb, GemmParams prm, const GemmDst *pd, unsigned flags,
-             void *workspace, size_t workspace_bytes, int *status, int force_bn = 0) {
+             void *workspace, size_t workspace_bytes, int *status, int force_bn = 0,
+             const GemmDstTma *pt = nullptr) {
   if (M <= 0 || N <= 0 || K <= 0 || !A || !B) return kErrInvalidArg;
   if (lda < K || ldb < N) return kErrInvalidArg;
   if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 30))
@@ -817,7 +885,7 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   GemmPlan g = plan_gemm(M, N, K, force_bn);
   // Split-K only where its epilogue applies: a plain product written to C
   // (no C read, bias, activation or fused exchange) in the split operand form.
-  if (g.ks > 1 && (pd || prm.beta != 0.0f || prm.bias || prm.act != 0 ||
+  if (g.ks > 1 && (pd || pt || prm.beta != 0.0f || prm.bias || prm.act != 0 ||
                    (flags & NPLK_GEMM_RAW_OPERANDS) || !workspace ||
                    workspace_bytes < g.a_bytes + g.b_bytes))
     g = plan_gemm(M, N, K, g.bn);
@@ -844,6 +912,7 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
   if ((flags & NPLK_GEMM_RAW_OPERANDS) && !raw_ok) return kErrUnsupported;
   const bool raw = (flags & NPLK_GEMM_RAW_OPERANDS) ||
                    (!have_ws && raw_ok && !(flags & NPLK_GEMM_SPLIT_OPERANDS));
+  if (raw && pt) return kErrUnsupported;  // the TMA-store exchange has the split form only
   if (raw) {
     if (g.bn == 128) return launch_gemm_raw<128>(s, g, A, lda, B, ldb, prm, pd);
     return launch_gemm_raw<64>(s, g, A, lda, B, ldb, prm, pd);
@@ -861,8 +930,8 @@ int gemm_run(cudaStream_t s, int64_t M, int64_t N, int64_t K, const float *A, in
                                        B, K, N, ldb, b_split, g.bn, g.n_blocks * g.bn, g.kp,
                                        g.ks > 1 ? prm.C : nullptr, prm.ldc);
   if (rc) return rc;
-  if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm, pd);
-  return launch_gemm<64>(s, g, a_split, b_split, prm, pd);
+  if (g.bn == 128) return launch_gemm<128>(s, g, a_split, b_split, prm, pd, pt);
+  return launch_gemm<64>(s, g, a_split, b_split, prm, pd, pt);
 }
 
 }  // namespace
@@ -915,6 +984,24 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
     vec = vec && (reinterpret_cast<uintptr_t>(dst[d]) & 15u) == 0;
   }
   pd.dst_vec = vec ? 1 : 0;
+  // TMA-store form when the destinations allow 16-byte aligned tensor maps and
+  // the split operand form runs (a workspace, not forced raw).
+  const bool tma = vec && !(flags & (NPLK_GEMM_RAW_OPERANDS | NPLK_GEMM_PEER_SM_STORES)) &&
+                   workspace && workspace_bytes >= nplk_gemm_workspace_size(M, N_local, K) &&
+                   M >= 32 && N_local >= 32 && M <= (int64_t(1) << 30) &&
+                   N_local <= (int64_t(1) << 30);
+  if (tma) {
+    GemmDstTma pt{};
+    pt.n_dst = n_dst;
+    pt.rot = pd.rot;
+    for (int d = 0; d < n_dst; ++d) {
+      const int rc = encode_tmap_2d_f32_sw128(&pt.map[d], dst[d] + col_offset, N_local, M,
+                                              ldc * 4, 32, 32);
+      if (rc) return rc;
+    }
+    return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm,
+                    nullptr, flags, workspace, workspace_bytes, status, 0, &pt);
+  }
   return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, &pd,
                   flags, workspace, workspace_bytes, status);
 }

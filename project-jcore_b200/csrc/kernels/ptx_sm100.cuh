@@ -151,6 +151,31 @@ __device__ __forceinline__ void bulk_load_g2s(void *dst, const void *src, uint32
       : "memory");
 }
 
+// TMA tensor store of the 2-D box at (x, y) of `map` from shared memory
+// (bulk-group completion; no multicast). The box's shared-memory image must be
+// laid out as the map's swizzle mode expects.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *smem_src, int x,
+                                             int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   map),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until at most N committed bulk groups of this thread still read their
+// shared-memory source (their global writes may still be in flight).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Waits until at most N committed bulk groups of this thread are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Makes this thread's generic-proxy shared-memory writes visible to the async
 // proxy (tensor-core operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem() {

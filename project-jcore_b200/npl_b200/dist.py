@@ -172,7 +172,7 @@ class PeerBuffers:
 
 
 def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=None,
-                              act: int = 0, barrier_before: bool = False):
+                              act: int = 0, barrier_before: bool = False, flags: int = 0):
     """C = act(A @ B + bias) with B column-sharded, written by every rank
     straight into every rank's C (``peers.tensor``, row-major [M][N]) by the
     GEMM epilogue (nplk_gemm_allgather). Asynchronous on the current stream.
@@ -187,7 +187,9 @@ def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=Non
         barrier before each call (``barrier_before=True`` synchronises this
         rank's device and then barriers the process group), or order the
         calls by a barrier the caller already has (one per iteration after
-        the completion barrier above suffices)."""
+        the completion barrier above suffices).
+    ``flags`` go to nplk_gemm_allgather (NPLK_GEMM_PEER_SM_STORES: the epilogue
+    threads store into the peers instead of the TMA unit)."""
     import torch
     import torch.distributed as dist
 
@@ -209,7 +211,7 @@ def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=Non
     bias_ptr = C.c_void_p(bias.data_ptr() + c0 * bias.element_size()) if bias is not None else None
     rc = lib.nplk_gemm_allgather(stream, M, w, K, 1.0, C.c_void_p(A.data_ptr()), K,
                                  C.c_void_p(b_ptr), N, bias_ptr, act, 0.0, dst, peers.world, c0,
-                                 N, 0, C.c_void_p(workspace.data_ptr()), ws, None)
+                                 N, flags, C.c_void_p(workspace.data_ptr()), ws, None)
     if rc != 0:
         raise RuntimeError(f"nplk_gemm_allgather failed: {rc}")
     return peers.tensor

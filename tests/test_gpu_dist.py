@@ -43,15 +43,8 @@ def test_column_sharded_gemm_simulated_4_ranks():
     assert S.normwise_err(one.cpu().numpy(), full.cpu().numpy()) < 1e-6
 
 
-@pytest.mark.parametrize("g,M,K,w,act,raw", [(4, 300, 200, 96, 0, True), (3, 129, 64, 50, 1, False),
-                                             (2, 64, 4096, 256, 0, False)])
-def test_gemm_allgather_fused_epilogue_simulated(g, M, K, w, act, raw):
-    # The fused GEMM + all-gather on one device: g buffers stand for the g
-    # ranks' C; each "rank" computes its column block and its epilogue stores
-    # the block into all g buffers, which must all end up holding the whole
-    # C = act(A @ B + bias), bit for bit alike.
+def _allgather_simulated(lib, g, M, K, w, act, form):
     import torch
-    lib = S.gpu_lib()
     gen = torch.Generator(device="cuda").manual_seed(g * M + w)
     N = g * w
     A = torch.randn(M, K, device="cuda", generator=gen)
@@ -59,24 +52,52 @@ def test_gemm_allgather_fused_epilogue_simulated(g, M, K, w, act, raw):
     bias = torch.randn(N, device="cuda", generator=gen) * 0.1
     Cs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(g)]
     dst = (C.c_void_p * g)(*[c.data_ptr() for c in Cs])
+    raw = form == "raw"
+    flags = {"raw": nb.NPLK_GEMM_RAW_OPERANDS, "sm": nb.NPLK_GEMM_PEER_SM_STORES, "tma": 0}[form]
     ws = 0 if raw else lib.nplk_gemm_workspace_size(M, w, K)
     work = torch.empty(ws // 4 + 64, device="cuda") if ws else None
     for r in range(g):
         rc = lib.nplk_gemm_allgather(
             S.cuda_stream(), M, w, K, 1.0, S.dptr(A), K, C.c_void_p(B.data_ptr() + 4 * r * w), N,
-            C.c_void_p(bias.data_ptr() + 4 * r * w), act, 0.0, dst, g, r * w, N,
-            nb.NPLK_GEMM_RAW_OPERANDS if raw else 0,
+            C.c_void_p(bias.data_ptr() + 4 * r * w), act, 0.0, dst, g, r * w, N, flags,
             S.dptr(work) if work is not None else None, ws, None)
         assert rc == 0, rc
     torch.cuda.synchronize()
     assert lib.nplk_read_status(S.cuda_stream()) == 0
+    return A, B, bias, [c.cpu().numpy() for c in Cs]
+
+
+# "tma": the default exchange through the TMA unit (w a multiple of 4); "sm":
+# stores from the epilogue threads; w = 50 takes the thread stores either way.
+@pytest.mark.parametrize("g,M,K,w,act,form", [(4, 300, 200, 96, 0, "raw"), (3, 129, 64, 50, 1, "tma"),
+                                              (2, 64, 4096, 256, 0, "tma"),
+                                              (3, 300, 160, 100, 1, "tma"),
+                                              (3, 300, 160, 100, 1, "sm"),
+                                              (2, 70, 96, 36, 0, "tma"),
+                                              (8, 257, 128, 64, 0, "tma")])
+def test_gemm_allgather_fused_epilogue_simulated(g, M, K, w, act, form):
+    # The fused GEMM + all-gather on one device: g buffers stand for the g
+    # ranks' C; each "rank" computes its column block and its epilogue stores
+    # the block into all g buffers, which must all end up holding the whole
+    # C = act(A @ B + bias), bit for bit alike (ragged rows and column blocks
+    # included: the TMA unit clips its boxes at the block's edges).
+    lib = S.gpu_lib()
+    A, B, bias, Cs = _allgather_simulated(lib, g, M, K, w, act, form)
     ref = A.double().cpu().numpy() @ B.double().cpu().numpy() + bias.double().cpu().numpy()
     if act:
         ref = np.maximum(ref, 0.0)
-    first = Cs[0].cpu().numpy()
+    first = Cs[0]
+    assert not np.isnan(first).any()
     assert S.normwise_err(first, ref) < 1e-4
     for c in Cs[1:]:
-        assert np.array_equal(c.cpu().numpy(), first)
+        assert np.array_equal(c, first)
+
+
+def test_gemm_allgather_tma_and_thread_stores_agree():
+    lib = S.gpu_lib()
+    _, _, _, tma = _allgather_simulated(lib, 4, 300, 256, 128, 1, "tma")
+    _, _, _, sm = _allgather_simulated(lib, 4, 300, 256, 128, 1, "sm")
+    assert np.array_equal(tma[0], sm[0]) and np.array_equal(tma[3], sm[3])
 
 
 def _free_port():
