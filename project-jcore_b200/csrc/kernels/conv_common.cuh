@@ -87,28 +87,34 @@ __device__ __forceinline__ void conv_store_chunk(float *__restrict__ y, int64_t 
 // kPair: the accumulator belongs to a CTA pair (conv_window_pair.cu); the
 // wait acquires at cluster scope and a timeout also raises the peer's abort
 // flag (`peer_abort`, its shared::cluster address).
+// `bar_id` names the 128-thread barrier of the draining warpgroup (a kernel
+// with several draining warpgroups gives each its own id and constants area).
 template <int BNC, int kAct, bool kPair = false>
 __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t acc_tmem,
                                                    int quad, int lane, int et, int mb, int nb,
                                                    float4 *ep_s, float *ep_beta_s,
                                                    uint64_t *acc_full, uint32_t acc_phase,
                                                    volatile int *abort_flag,
-                                                   uint32_t peer_abort = 0u) {
-  if constexpr (kPair)
-    mbar_wait_pair(acc_full, acc_phase, abort_flag, peer_abort, p.status, kStatusTimeoutEpilogue);
-  else
-    mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
-  // All four warps pass this barrier before anyone rewrites the constants of
-  // the previous tile, and they leave together if the CTA aborted.
-  named_barrier_sync(1, 128);
-  if (*abort_flag) return false;
+                                                   uint32_t peer_abort = 0u, int bar_id = 1) {
+  // The tile's constants are staged before the accumulator wait, so their
+  // loads overlap the MMAs still accumulating the tile (for a CTA's last tile
+  // they would otherwise follow its last MMA). All four warps pass the first
+  // barrier before anyone rewrites the constants of the previous tile.
+  named_barrier_sync(bar_id, 128);
   for (int i = et; i < BNC; i += 128) {
     const int co = nb * BNC + i;
     ep_s[i] = make_float4(p.ep[kEpBias * p.cout_pad + co], p.ep[kEpMean * p.cout_pad + co],
                           p.ep[kEpGamma * p.cout_pad + co], p.ep[kEpInvStd * p.cout_pad + co]);
     ep_beta_s[i] = p.ep[kEpBeta * p.cout_pad + co];
   }
-  named_barrier_sync(1, 128);
+  if constexpr (kPair)
+    mbar_wait_pair(acc_full, acc_phase, abort_flag, peer_abort, p.status, kStatusTimeoutEpilogue);
+  else
+    mbar_wait(acc_full, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue);
+  // The four warps leave together if the CTA aborted, and the constants are
+  // visible to all of them past this barrier.
+  named_barrier_sync(bar_id, 128);
+  if (*abort_flag) return false;
   tc_fence_after_sync();
   const int m = mb * kConvBM + quad * 32 + lane;  // GEMM row (virtual pixel)
   bool valid = m < p.Mv;

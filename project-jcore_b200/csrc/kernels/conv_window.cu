@@ -66,7 +66,11 @@ struct ConvWinTraits {
   static constexpr int kAccPerPipe = 2;
   static constexpr int kTmemCols = kPipes * kAccPerPipe * kAccCols;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kSmemBytes = 1024 + kPipeBytes + kBarrierBytes + BNC * 20;
+  // Per-channel epilogue constants (float4 + beta per channel) for each
+  // draining warpgroup: the epilogue warps, then each pipeline's window
+  // warpgroup, which drains its pipeline's last tile.
+  static constexpr int kEpConstBytes = BNC * 20;
+  static constexpr int kSmemBytes = 1024 + kPipeBytes + kBarrierBytes + (1 + kPipes) * kEpConstBytes;
   static_assert(kTmemCols == 512, "TMEM budget");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -104,8 +108,11 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   uint64_t *never = acc_empty + P * T::kAccPerPipe;  // never arrived on (injected_stall)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(never + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  float4 *ep_s = reinterpret_cast<float4 *>(bars + T::kBarrierBytes);
-  float *ep_beta_s = reinterpret_cast<float *>(ep_s + BNC);
+  // Epilogue constants of draining warpgroup g (0: the epilogue warps, 1 + p:
+  // the window warpgroup of pipeline p).
+  auto ep_area = [&](int g) {
+    return reinterpret_cast<float4 *>(bars + T::kBarrierBytes + g * T::kEpConstBytes);
+  };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -141,6 +148,39 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
   const int num_tiles = p.m_blocks * p.n_blocks;
   const int cblocks = p.C / kConvBK;
   const int win_bytes = wg.win_rows * kConvBK * 4;
+  // Drains this CTA's local tile j (tile blockIdx.x + j * gridDim.x, run by
+  // pipeline j % P) with a warpgroup of four warps (quad = TMEM lane quadrant,
+  // et = 0..127): draining warpgroup g, named barrier bar_id. False when the
+  // CTA aborted.
+  auto drain_tile = [&](int j, int quad, int et, int g, int bar_id) -> bool {
+    const int tile = blockIdx.x + j * static_cast<int>(gridDim.x);
+    const int jj = j / P;
+    const int acc = (j % P) * T::kAccPerPipe + (jj & 1);
+    const uint32_t acc_phase = (jj >> 1) & 1;
+    const int mb = tile / p.n_blocks;
+    const int nb = tile - mb * p.n_blocks;
+    float4 *ep_s = ep_area(g);
+    if (!conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb, nb,
+                                       ep_s, reinterpret_cast<float *>(ep_s + BNC),
+                                       &acc_full[acc], acc_phase, abort_flag, 0u, bar_id))
+      return false;
+    tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    return true;
+  };
+  // Window warpgroup of pipeline `pipe`, after its last window: drains the
+  // pipeline's last tile, so that the CTA's final tiles drain in parallel
+  // rather than one after another in the epilogue warps.
+  auto drain_last_tile = [&](int pipe) -> bool {
+    const int first = blockIdx.x + pipe * static_cast<int>(gridDim.x);
+    if (first >= num_tiles) return true;
+    const int step = P * static_cast<int>(gridDim.x);
+    const int jj_last = (num_tiles - 1 - first) / step;
+    const int et = threadIdx.x - (T::kFirstCvtWarp + 4 * pipe) * 32;
+    griddep_wait();  // the epilogue constants may come from the preparation just before
+    return drain_tile(pipe + P * jj_last, warp & 3, et, 1 + pipe, 2 + pipe);
+  };
   // Local tile j of this CTA is tile blockIdx.x + j*gridDim.x; pipeline j % P
   // runs it. Per tile: windows (cb, kh, kw group) in that order, each
   // followed by its taps_per_win weight slabs.
@@ -382,6 +422,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
         }
       }
     }
+    if (!drain_last_tile(pipe)) goto role_done;
   } else if (warp < T::kFirstEpiWarp) {
     // ---------------- converter warpgroup of pipeline `pipe`: lo = x - trunc(x) ----------------
     const int pipe = (warp - T::kFirstCvtWarp) >> 2;
@@ -420,6 +461,7 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
         }
       }
     }
+    drain_last_tile(pipe);
   cvt_done:;
   } else {
     // ---------------- epilogue (4 warps, one per TMEM lane quadrant) ----------------
@@ -428,18 +470,9 @@ __global__ void __launch_bounds__(ConvWinTraits<BNC, kGather>::kThreads, 1)
     griddep_wait();  // the epilogue constants, likewise
     int j = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++j) {
-      const int pipe = j % P;
-      const int jj = j / P;
-      const int acc = pipe * T::kAccPerPipe + (jj & 1);
-      const uint32_t acc_phase = (jj >> 1) & 1;
-      const int mb = tile / p.n_blocks;
-      const int nb = tile - mb * p.n_blocks;
-      if (!conv_epilogue_tile<BNC, kAct>(p, tmem_base + acc * T::kAccCols, quad, lane, et, mb, nb,
-                                         ep_s, ep_beta_s, &acc_full[acc], acc_phase, abort_flag))
-        break;
-      tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      // A pipeline's last tile is drained by its window warpgroup.
+      if (tile + P * static_cast<int>(gridDim.x) >= num_tiles) continue;
+      if (!drain_tile(j, quad, et, 0, 1)) break;
     }
   }
 
