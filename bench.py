@@ -107,8 +107,14 @@ class ClockSampler:
         self.dev = device_index
         self.proc = None
         self.file = None
+        # The NVML poll runs from construction on (its first samples take a
+        # few milliseconds, longer than the timed region); start() marks the
+        # window whose samples are reported.
+        self.nvml = NvmlClockPoller(device_index)
+        self.nvml.start()
 
     def start(self):
+        self.nvml.mark()
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -119,8 +125,9 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        fine = self.nvml.stop()
         if not self.proc:
-            return None
+            return fine
         time.sleep(0.25)
         self.proc.terminate()
         try:
@@ -146,9 +153,107 @@ class ClockSampler:
                 if flag.lower() == "active":
                     reasons.add(name)
         if not sm:
+            return fine
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm), "source": "nvidia-smi -lms 200"}
+        if fine and fine["samples"] >= len(sm):
+            # The timed region is only milliseconds long: the NVML poll sees
+            # it at sub-millisecond intervals, nvidia-smi at most once or twice.
+            out.update({"sm_mhz": fine["sm_mhz"], "sm_mhz_min": fine["sm_mhz_min"],
+                        "samples": fine["samples"], "source": fine["source"],
+                        "reasons": sorted(set(out["reasons"]) | set(fine["reasons"])),
+                        "nvidia_smi": {"sm_mhz": statistics.median(sm), "samples": len(sm)}})
+            if fine.get("sm_max_mhz"):
+                out["sm_max_mhz"] = fine["sm_max_mhz"]
+        return out
+
+
+class NvmlClockPoller:
+    """Reads the SM clock and the active clock-event (throttle) reasons through
+    NVML in a background thread every ~0.5 ms while the timed region runs.
+    Read-only: it changes no clock or other setting. The device is found by
+    the PCI bus id torch reports for `device_index`."""
+
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int, interval_s: float = 0.0002):
+        self.dev = device_index
+        self.interval = interval_s
+        self.thread = None
+        self.samples = []  # (perf_counter time, MHz, reason bits)
+        self.stop_flag = False
+        self.handle = None
+        self.max_mhz = None
+        self.window = None
+
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.dev)
+        try:
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except (AttributeError, pynvml.NVMLError):
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        return pynvml
+
+    def start(self):
+        import threading
+        try:
+            nv = self._open()
+        except Exception:  # no NVML (or no device): nvidia-smi alone records clocks
+            self.handle = None
+            return
+
+        def poll():
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self.stop_flag:
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                    rs = get_reasons(self.handle)
+                except Exception:
+                    break
+                self.samples.append((time.perf_counter(), mhz, rs))
+                time.sleep(self.interval)
+
+        self.stop_flag = False
+        # The timed region lasts milliseconds while the launching thread holds
+        # the interpreter lock between its calls; a short switch interval lets
+        # this thread take its samples meanwhile (restored in stop()).
+        self.saved_switch = sys.getswitchinterval()
+        sys.setswitchinterval(0.0001)
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+
+    def mark(self):
+        """Start of the timed region: samples before it are not reported."""
+        self.window = time.perf_counter()
+
+    def stop(self):
+        if self.thread is None:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        t_end = time.perf_counter()
+        self.stop_flag = True
+        self.thread.join(timeout=5)
+        sys.setswitchinterval(self.saved_switch)
+        t_start = self.window if self.window is not None else 0.0
+        inside = [(m, rs) for t, m, rs in self.samples if t_start <= t <= t_end]
+        if not inside:
+            return None
+        mhz = [m for m, _ in inside]
+        reasons = set()
+        for _, rs in inside:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(mhz), "sm_mhz_min": min(mhz),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(mhz), "source": "NVML poll every ~0.2 ms during the timed region"}
 
 
 # ---------------------------------------------------------------------------
@@ -405,6 +510,9 @@ def run_b200(args, rank, world, local_rank):
                                   p(tb), 1e-5, nb.NPL_ACT_RELU, 0.0, p(ty), p(work), ws, None)
         assert r == 0, r
 
+    # clock sampling: the NVML poll starts before the warm-up and reports the
+    # samples taken inside the timed region
+    sampler = ClockSampler(local_rank) if rank == 0 else None
     for _ in range(args.warmup):
         flush()
         fused()
@@ -413,7 +521,6 @@ def run_b200(args, rank, world, local_rank):
         raise RuntimeError("conv kernel reported a pipeline timeout")
 
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
-    sampler = ClockSampler(local_rank) if rank == 0 else None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -1051,9 +1158,9 @@ def gemm_dist(args, rank, world, local_rank):
     # C over NVLink (CUDA IPC peer pointers); C is complete on every rank when
     # all ranks' kernels have finished, i.e. after the max over ranks of the
     # per-rank device time.
-    # The peers are written through the TMA unit (the default) and, for
-    # comparison, by 16-byte stores from the epilogue threads; C is checked
-    # after the TMA form, which runs last.
+    # The peers are written by 16-byte stores from the epilogue threads (the
+    # default) and, for comparison, through the TMA unit; C is checked after
+    # the default form, which runs last.
     full_f = torch.empty(GEMM_M, GEMM_N, device=dev)
     peers = nd.PeerBuffers(full_f, world, rank)
 
@@ -1077,7 +1184,7 @@ def gemm_dist(args, rank, world, local_rank):
         return tf.item()
 
     try:
-        sm_ms = fused_ms(nb.NPLK_GEMM_PEER_SM_STORES)
+        tma_ms = fused_ms(nb.NPLK_GEMM_PEER_TMA_STORES)
         fm = fused_ms(0)
         ferr = ((full_f[rows].double() - ref).abs().max() / ref.abs().max()).item()
     finally:
@@ -1120,13 +1227,13 @@ def gemm_dist(args, rank, world, local_rank):
                       "c_max_normwise_diff_all_ranks": float(diff.item()),
                       "peer_egress_bytes_per_rank": egress,
                       "peer_egress_GB/s_per_rank": round(egress / (fm / 1e3) / 1e9, 1),
-                      "step": "nplk_gemm_allgather: the GEMM epilogue hands every 32x32 piece "
-                              "to the TMA unit, which stores it into all ranks' C over NVLink "
-                              "(CUDA IPC peer pointers)",
-                      "thread_stores": {"ms": round(sm_ms, 4),
-                                        "value": round(GEMM_FLOPS / (sm_ms / 1e3) / 1e12, 2),
-                                        "step": "the same with 16-byte stores from the epilogue "
-                                                "threads (NPLK_GEMM_PEER_SM_STORES)"}},
+                      "step": "nplk_gemm_allgather: the GEMM epilogue stores every tile into "
+                              "all ranks' C over NVLink (CUDA IPC peer pointers) with 16-byte "
+                              "stores from its threads",
+                      "tma_stores": {"ms": round(tma_ms, 4),
+                                     "value": round(GEMM_FLOPS / (tma_ms / 1e3) / 1e12, 2),
+                                     "step": "the same with one TMA tensor store per 32x32 piece "
+                                             "and destination (NPLK_GEMM_PEER_TMA_STORES)"}},
             "normwise_err_sampled_rows": err}
 
 

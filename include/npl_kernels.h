@@ -57,11 +57,14 @@ extern "C" {
  * do not qualify). */
 #define NPLK_GEMM_SPLIT_OPERANDS 2u
 #define NPLK_GEMM_RAW_OPERANDS 4u
-/* nplk_gemm_allgather: store into the destinations from the epilogue threads
- * (16-byte stores) instead of through the TMA unit (the default whenever the
- * destinations are 16-byte aligned with ldc and col_offset multiples of 4 and
- * the split operand form runs). Both give the same C. */
-#define NPLK_GEMM_PEER_SM_STORES 8u
+/* nplk_gemm_allgather: store into the destinations through the TMA unit (one
+ * tensor store per 32 x 32 piece and destination) instead of with 16-byte
+ * stores from the epilogue threads (the default). Taken when the destinations
+ * are 16-byte aligned with ldc and col_offset multiples of 4 and the split
+ * operand form runs; otherwise the thread stores run. Both give the same C;
+ * measured slower on 2 and 8 B200s (8192 x 16384 x 4096 column-sharded:
+ * 1.094 vs 1.031 ms at 8 GPUs). */
+#define NPLK_GEMM_PEER_TMA_STORES 8u
 
 /* ---- dense contractions (tcgen05, 3xTF32) ---------------------------------- */
 
@@ -310,10 +313,10 @@ NPL_API int nplk_ipc_close_handle(void *dev_ptr, uint64_t offset);
  * usual layout (dst[] in rank order, col_offset = rank * N_local) each rank
  * visits the destinations starting after its own index, so the ranks' stores
  * spread over all peers instead of converging on one; any order gives the
- * same C. The epilogue hands each 32 x 32 piece to the TMA unit once per
- * destination (NPLK_GEMM_PEER_SM_STORES: 16-byte stores from the epilogue
- * threads instead), so the NVLink writes drain while the next piece is formed.
- * beta is 0 (C is not read); other arguments as nplk_gemm. */
+ * same C. The epilogue stages each warp's 32 x 32 piece in shared memory and
+ * stores it to every destination with 16-byte stores that cover whole
+ * 128-byte row segments (NPLK_GEMM_PEER_TMA_STORES: one TMA tensor store per
+ * piece and destination instead). beta is 0 (C is not read); other arguments as nplk_gemm. */
 NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
                                 float alpha, const float *A, int64_t lda, const float *B,
                                 int64_t ldb, const float *bias, int act, float act_alpha,

@@ -984,9 +984,10 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
     vec = vec && (reinterpret_cast<uintptr_t>(dst[d]) & 15u) == 0;
   }
   pd.dst_vec = vec ? 1 : 0;
-  // TMA-store form when the destinations allow 16-byte aligned tensor maps and
-  // the split operand form runs (a workspace, not forced raw).
-  const bool tma = vec && !(flags & (NPLK_GEMM_RAW_OPERANDS | NPLK_GEMM_PEER_SM_STORES)) &&
+  // TMA-store form on request, when the destinations allow 16-byte aligned
+  // tensor maps and the split operand form runs (a workspace, not forced raw).
+  const bool tma = vec && (flags & NPLK_GEMM_PEER_TMA_STORES) &&
+                   !(flags & NPLK_GEMM_RAW_OPERANDS) &&
                    workspace && workspace_bytes >= nplk_gemm_workspace_size(M, N_local, K) &&
                    M >= 32 && N_local >= 32 && M <= (int64_t(1) << 30) &&
                    N_local <= (int64_t(1) << 30);

@@ -38,7 +38,7 @@ NPLK_CONV_ALGO_WINDOW, NPLK_CONV_ALGO_WINDOW_GATHER, NPLK_CONV_ALGO_WINDOW_PAIR 
 NPLK_GEMM_TF32_FAST = 1
 NPLK_GEMM_SPLIT_OPERANDS = 2
 NPLK_GEMM_RAW_OPERANDS = 4
-NPLK_GEMM_PEER_SM_STORES = 8
+NPLK_GEMM_PEER_TMA_STORES = 8
 NPLK_DEBUG_GEMM, NPLK_DEBUG_CONV_WINDOW = 1, 2
 NPLK_STATUS_TIMEOUT_MMA = 102
 

@@ -188,8 +188,8 @@ def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=Non
         rank's device and then barriers the process group), or order the
         calls by a barrier the caller already has (one per iteration after
         the completion barrier above suffices).
-    ``flags`` go to nplk_gemm_allgather (NPLK_GEMM_PEER_SM_STORES: the epilogue
-    threads store into the peers instead of the TMA unit)."""
+    ``flags`` go to nplk_gemm_allgather (NPLK_GEMM_PEER_TMA_STORES: the TMA
+    unit stores into the peers instead of the epilogue threads)."""
     import torch
     import torch.distributed as dist
 

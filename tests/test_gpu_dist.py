@@ -53,7 +53,7 @@ def _allgather_simulated(lib, g, M, K, w, act, form):
     Cs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(g)]
     dst = (C.c_void_p * g)(*[c.data_ptr() for c in Cs])
     raw = form == "raw"
-    flags = {"raw": nb.NPLK_GEMM_RAW_OPERANDS, "sm": nb.NPLK_GEMM_PEER_SM_STORES, "tma": 0}[form]
+    flags = {"raw": nb.NPLK_GEMM_RAW_OPERANDS, "sm": 0, "tma": nb.NPLK_GEMM_PEER_TMA_STORES}[form]
     ws = 0 if raw else lib.nplk_gemm_workspace_size(M, w, K)
     work = torch.empty(ws // 4 + 64, device="cuda") if ws else None
     for r in range(g):
@@ -67,14 +67,17 @@ def _allgather_simulated(lib, g, M, K, w, act, form):
     return A, B, bias, [c.cpu().numpy() for c in Cs]
 
 
-# "tma": the default exchange through the TMA unit (w a multiple of 4); "sm":
-# stores from the epilogue threads; w = 50 takes the thread stores either way.
+# "sm": the default exchange, 16-byte stores from the epilogue threads; "tma":
+# NPLK_GEMM_PEER_TMA_STORES, through the TMA unit (w a multiple of 4; w = 50
+# takes the thread stores either way).
 @pytest.mark.parametrize("g,M,K,w,act,form", [(4, 300, 200, 96, 0, "raw"), (3, 129, 64, 50, 1, "tma"),
                                               (2, 64, 4096, 256, 0, "tma"),
+                                              (2, 64, 4096, 256, 0, "sm"),
                                               (3, 300, 160, 100, 1, "tma"),
                                               (3, 300, 160, 100, 1, "sm"),
                                               (2, 70, 96, 36, 0, "tma"),
-                                              (8, 257, 128, 64, 0, "tma")])
+                                              (8, 257, 128, 64, 0, "tma"),
+                                              (8, 257, 128, 64, 0, "sm")])
 def test_gemm_allgather_fused_epilogue_simulated(g, M, K, w, act, form):
     # The fused GEMM + all-gather on one device: g buffers stand for the g
     # ranks' C; each "rank" computes its column block and its epilogue stores
