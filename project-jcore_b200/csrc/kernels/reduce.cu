@@ -85,61 +85,6 @@ __global__ void softmax_rows_warp_kernel(const float *__restrict__ x, float *__r
   }
 }
 
-// The same for rows of at most 32 * 4 * NV elements, software-pipelined: a
-// warp issues the loads of its next row before it reduces and writes the
-// current one, so loads stay in flight through the reductions (one warp
-// per row otherwise leaves HBM idle while it computes). Same arithmetic and
-// order as softmax_rows_warp_kernel.
-template <int NV>
-__global__ void softmax_rows_pipelined_kernel(const float *__restrict__ x, float *__restrict__ y,
-                                              int64_t rows, int cols) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  const int c4 = cols >> 2;
-  float4 cur[NV], nxt[NV];
-  auto load = [&](int64_t r, float4 (&v)[NV]) {
-    const float4 *xr = reinterpret_cast<const float4 *>(x + r * cols);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = lane + 32 * i;
-      v[i] = j < c4 ? __ldg(xr + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    }
-  };
-  if (warp_id < rows) load(warp_id, cur);
-  for (int64_t r = warp_id; r < rows; r += nwarps) {
-    const int64_t rn = r + nwarps;
-    if (rn < rows) load(rn, nxt);
-    float mx = -CUDART_INF_F;
-#pragma unroll
-    for (int i = 0; i < NV; ++i)
-      if (lane + 32 * i < c4)
-        mx = fmaxf(mx, fmaxf(fmaxf(cur[i].x, cur[i].y), fmaxf(cur[i].z, cur[i].w)));
-    mx = warp_max(mx);
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (lane + 32 * i < c4) {
-        cur[i].x = expf(cur[i].x - mx);
-        cur[i].y = expf(cur[i].y - mx);
-        cur[i].z = expf(cur[i].z - mx);
-        cur[i].w = expf(cur[i].w - mx);
-        sum += (cur[i].x + cur[i].y) + (cur[i].z + cur[i].w);
-      }
-    }
-    sum = warp_sum(sum);
-    float4 *yr = reinterpret_cast<float4 *>(y + r * cols);
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = lane + 32 * i;
-      if (j < c4)
-        yr[j] = make_float4(cur[i].x / sum, cur[i].y / sum, cur[i].z / sum, cur[i].w / sum);
-    }
-#pragma unroll
-    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
-  }
-}
-
 // General softmax: one thread per (outer, inner) line, strided along the
 // axis; consecutive threads take consecutive inner indices (coalesced).
 __global__ void softmax_strided_kernel(const float *__restrict__ x, float *__restrict__ y,
@@ -522,12 +467,17 @@ extern "C" int nplk_softmax(void *stream, int64_t outer, int64_t axis_len, int64
       aligned16(y)) {
     const int c4 = static_cast<int>(axis_len / 4);
     const int threads = 256;
-    const int grid = grid_for(outer, threads / 32);
+    // One warp per row and a grid that covers every row: block scheduling
+    // keeps the loads of many rows in flight (rows of 1000: 120.8 us against
+    // 156.7 us for a grid of 16 blocks per SM whose warps each pipelined
+    // several rows).
+    const int64_t blocks = ceil_div(outer, static_cast<int64_t>(threads / 32));
+    const int grid = static_cast<int>(blocks < (int64_t(1) << 30) ? blocks : (int64_t(1) << 30));
     const int cols = static_cast<int>(axis_len);
     if (c4 <= 32 * 4)
       softmax_rows_warp_kernel<4><<<grid, threads, 0, s>>>(x, y, outer, cols);
     else if (c4 <= 32 * 8)
-      softmax_rows_pipelined_kernel<8><<<grid, threads, 0, s>>>(x, y, outer, cols);
+      softmax_rows_warp_kernel<8><<<grid, threads, 0, s>>>(x, y, outer, cols);
     else
       softmax_rows_warp_kernel<16><<<grid, threads, 0, s>>>(x, y, outer, cols);
   } else {
