@@ -759,6 +759,20 @@ def bandwidth_also(lib, local_rank, reps=10):
 
             cases.append(("chain depthwise->BN->ReLU->GAP->softmax [256,512,14,14]", chain_bytes,
                           chain))
+        # The same chain with its first four calls in one pass
+        # (nplk_depthwise_bn_act_gap, no intermediate map written), then the
+        # softmax; bytes: x and the filters read once, the pooled [N,C] written,
+        # the softmax's read and write.
+        fgap = torch.empty(n * c, device=dev)
+        fsm = torch.empty(n * c, device=dev)
+        fused_bytes = nx * 4 + w.numel() * 4 + n * c * 4 + n * c * 8
+
+        def chain_fused():
+            return abs(workloads.bandwidth_chain_fused(lib, s, x, w, bn[0], bn[1], bn[2], bn[3],
+                                                       fgap.view(n, c), fsm.view(n, c)))
+
+        cases.append(("chain fused: depthwise+BN+ReLU+GAP in one pass, then softmax "
+                      "[256,512,14,14]", fused_bytes, chain_fused))
         cases += [
             ("device copy of the same tensor (reference)", nx * 8, lambda: (y.copy_(x), 0)[1]),
             ("read (sum) of the same tensor (reference)", nx * 4,
@@ -1049,6 +1063,20 @@ def strong_scaling_also(lib, rank, world, local_rank, reps=10):
                 assert r == 0, r
         return fn
 
+    def chain_fused_case(n):
+        gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+        x = torch.randn(n, 512, 14, 14, device=dev, generator=gen)
+        wgen = torch.Generator(device=dev).manual_seed(8)
+        w = torch.randn(512, 1, 3, 3, device=dev, generator=wgen) * 0.3
+        bn = [torch.rand(512, device=dev, generator=wgen) + 0.5 for _ in range(4)]
+        gap, probs = torch.empty(n, 512, device=dev), torch.empty(n, 512, device=dev)
+
+        def fn():
+            r = workloads.bandwidth_chain_fused(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], gap,
+                                                probs)
+            assert r == 0, r
+        return fn
+
     def chain_case(n):
         gen = torch.Generator(device=dev).manual_seed(2000 + rank)
         x = torch.randn(n, 512, 14, 14, device=dev, generator=gen)
@@ -1074,6 +1102,8 @@ def strong_scaling_also(lib, rank, world, local_rank, reps=10):
         ("depthwise->BN->ReLU->GAP->softmax N=256 C=512 14x14", 256, "GB/s",
          lambda n: n * 720914432 / 256 / 1e9,
          lambda n: chain_case(n)),
+        ("the same chain fused (depthwise+BN+ReLU+GAP in one pass, then softmax)", 256,
+         "images/s", lambda n: n, lambda n: chain_fused_case(n)),
     ]
     out = {}
     for name, n_total, unit, work_of, make in cases:

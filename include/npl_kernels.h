@@ -221,6 +221,24 @@ NPL_API int nplk_conv2d_maxpool_fused(void *stream, const nplk_conv_geom_t *g, c
 NPL_API int nplk_depthwise_conv2d(void *stream, const nplk_conv_geom_t *g, const float *x,
                           const float *w, const float *bias, float *out);
 
+/* npl_depthwise_conv2d -> npl_batch_norm (inference) -> npl_activation ->
+ * npl_global_avg_pool in one pass (npl_convolution.cpp:60-90,
+ * npl_activation_norm.cpp:118-153 and :51-54, npl_pooling.cpp:63-87):
+ * gap[n*C + c] = mean over the output plane of
+ * act(gamma*((dw(x) + bias) - mean)*rsd + beta), rsd = 1/sqrt(var+eps), with
+ * the activation codes of nplk_activation (0..10). y, when not NULL, also
+ * receives the activated map [N,C,Ho,Wo]; the depthwise and BN maps are never
+ * written. Every value equals what nplk_depthwise_conv2d, nplk_batch_norm_infer,
+ * nplk_activation and nplk_global_avg_pool give run one after another, bit for
+ * bit. Weights [C,1,kh,kw], g->c_out == g->c_in; gamma, beta, bias may be
+ * NULL (1, 0, none). NPL_ERR_UNSUPPORTED unless H*W <= 1024 and Ho*Wo <= 512
+ * are multiples of 4 and x (and y) are 16-byte aligned: callers then run the
+ * four calls. */
+NPL_API int nplk_depthwise_bn_act_gap(void *stream, const nplk_conv_geom_t *g, const float *x,
+                                      const float *w, const float *bias, const float *mean,
+                                      const float *var, const float *gamma, const float *beta,
+                                      float eps, int act, float act_alpha, float *y, float *gap);
+
 /* Inference batch norm over NCHW planes: y = gamma*(x-mean)*rsd + beta with
  * rsd = 1/sqrt(var+eps) (npl_activation_norm.cpp:362-407). */
 NPL_API int nplk_batch_norm_infer(void *stream, int64_t n, int64_t c, int64_t hw, const float *x,

@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
+#include <numeric>
+
 #include "nplk_device.cuh"
 #include "nplk_host.h"
 #include "ptx_sm100.cuh"
@@ -573,6 +575,380 @@ int launch_band(cudaStream_t s, const float *x, const float *w, const float *bia
 }  // namespace nplk
 
 using namespace nplk;
+
+namespace nplk {
+
+// ---------------------------------------------------------------------------
+// Depthwise conv -> inference batch norm -> activation -> global average pool
+// in one pass (nplk_depthwise_bn_act_gap): the reference's
+// npl_depthwise_conv2d (npl_convolution.cpp:60-90, ExecuteDepthwiseConv
+// :904-991), npl_batch_norm (npl_activation_norm.cpp:118-153, the inference
+// form :389-398), npl_relu / npl_activation (:51-54) and npl_global_avg_pool
+// (npl_pooling.cpp:63-87) applied back to back, with the intermediate maps
+// never written to HBM unless asked for.
+//
+// One warp per NCHW plane: the input plane is staged in shared memory (16-byte
+// loads, all issued before the first store); lane l computes the outputs at
+// flat indices l, l + 32, ... (consecutive lanes read consecutive columns:
+// no bank conflicts), each with the depthwise kernel's sum (kh outer, kw
+// inner, padding skipped, then the bias), BN's expression and the
+// activation; the activated outputs go to a second shared-memory block, and
+// lane l then sums its float4 groups l, l + 32, ... in the GAP kernel's order (group by
+// group from 0, (a + b) + (c + d) within a group, then the warp butterfly),
+// storing them to y when asked. Every value is therefore the one the separate
+// kernels produce, bit for bit.
+// ---------------------------------------------------------------------------
+constexpr int kDwGapWarps = 8;       // planes per 256-thread block
+
+__device__ __forceinline__ float dwgap_warp_sum(float v) {  // the GAP kernel's butterfly
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+inline bool dwgap_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+constexpr int kDwGapMaxIn = 1024;    // input plane elements staged per warp (4 KB)
+
+// The activated plane, staged in shared memory, to y (when asked) and to its
+// average: lane l takes the float4 groups l, l + 32, ... in the GAP kernel's
+// order (gap_planes in reduce.cu).
+template <int J>
+__device__ __forceinline__ void dwgap_finish(const float *xsw, float *__restrict__ y,
+                                             float *__restrict__ gap, int64_t plane, int howo,
+                                             int lane) {
+  float s = 0.0f;
+  float4 *y4 = y ? reinterpret_cast<float4 *>(y + plane * howo) : nullptr;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int q = lane + 32 * j;
+    float4 o = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (4 * q < howo) {
+      o = reinterpret_cast<const float4 *>(xsw)[q];
+      if (y4) y4[q] = o;
+    }
+    s += (o.x + o.y) + (o.z + o.w);
+  }
+  s = dwgap_warp_sum(s);
+  if (lane == 0) gap[plane] = s / static_cast<float>(howo);
+}
+
+// J: output float4 groups per lane (output planes of <= 128 J elements);
+// JI: input float4 per lane (input planes of <= 128 JI elements); K3: 3x3
+// filter (unrolled taps), else any filter; kRelu: the activation is ReLU
+// (code 1), else any code of nplk_activation; SR > 0: 3x3, stride 1, pad 1,
+// same-size planes at most 32 wide, whose columns split into 32 / Wo
+// segments of SR rows: lane (column, segment) runs down its strip, reads each
+// input row's three columns once and folds them into the (up to three)
+// output rows they feed, in kh order; padding enters as zero products, which
+// leave a sum unchanged when the weights are finite (the depthwise kernel's
+// register path does the same), so planes with a non-finite weight take the
+// per-output path.
+// A channel's filter (3x3 unrolled) and bias, and its BN constants formed
+// exactly as bn_infer_kernel forms them.
+struct DwGapConsts {
+  float wk[9];
+  float bv, qg, qm, qi, qb;
+};
+template <bool K3>
+__device__ __forceinline__ void dwgap_consts(DwGapConsts &k, int c, const float *__restrict__ w,
+                                             const float *__restrict__ bias,
+                                             const float *__restrict__ mean,
+                                             const float *__restrict__ var,
+                                             const float *__restrict__ gamma,
+                                             const float *__restrict__ beta, float eps) {
+  if (K3) {
+#pragma unroll
+    for (int t = 0; t < 9; ++t) k.wk[t] = __ldg(w + c * 9 + t);
+  }
+  k.bv = bias ? __ldg(bias + c) : 0.0f;
+  k.qg = gamma ? __ldg(gamma + c) : 1.0f;
+  k.qm = __ldg(mean + c);
+  k.qi = 1.0f / sqrtf(__ldg(var + c) + eps);
+  k.qb = beta ? __ldg(beta + c) : 0.0f;
+}
+
+template <int J, bool K3, bool kRelu, int SR>
+__device__ __forceinline__ void dwgap_plane(
+    const float *xsw, float *xout, int64_t plane, int lane, const DwGapConsts &kc,
+    const float *__restrict__ wc, bool has_bias, int act, float act_alpha,
+    float *__restrict__ y, float *__restrict__ gap, const WindowGeom &g) {
+  const int howo = g.Ho * g.Wo;
+  const float(&wk)[9] = kc.wk;
+  const float bv = kc.bv, qg = kc.qg, qm = kc.qm, qi = kc.qi, qb = kc.qb;
+  const bool bias = has_bias;
+  __syncwarp();
+  if constexpr (SR > 0) {
+    bool finite = true;
+#pragma unroll
+    for (int t = 0; t < 9; ++t) finite = finite && isfinite(wk[t]);
+    if (finite) {
+      const int ow = lane % g.Wo, seg = lane / g.Wo;
+      const bool active = seg < 32 / g.Wo;
+      const int r0 = seg * SR;
+      float acc[SR];
+#pragma unroll
+      for (int r = 0; r < SR; ++r) acc[r] = 0.0f;
+#pragma unroll
+      for (int t = 0; t < SR + 2; ++t) {  // input rows r0 - 1 .. r0 + SR
+        const int ih = r0 - 1 + t;
+        const bool rin = active && static_cast<unsigned>(ih) < static_cast<unsigned>(g.H);
+        // indices clamped into the staged plane, so no address leaves it
+        const int base = (rin ? ih : 0) * g.W + ow;
+        const float v0 = (rin && ow > 0) ? xsw[base - (ow > 0 ? 1 : 0)] : 0.0f;
+        const float v1 = rin ? xsw[base] : 0.0f;
+        const float v2 = (rin && ow + 1 < g.W) ? xsw[base + (ow + 1 < g.W ? 1 : 0)] : 0.0f;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+          const int r = t - kh;  // output row r0 + r takes input row ih as its tap row kh
+          if (r >= 0 && r < SR) {
+            acc[r] += v0 * wk[kh * 3 + 0];
+            acc[r] += v1 * wk[kh * 3 + 1];
+            acc[r] += v2 * wk[kh * 3 + 2];
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < SR; ++r) {
+        float sum = acc[r];
+        if (bias) sum += bv;
+        const float t = qg * (sum - qm) * qi + qb;
+        acc[r] = kRelu ? (t < 0.0f ? 0.0f : t) : apply_act(t, act, act_alpha);
+      }
+#pragma unroll
+      for (int r = 0; r < SR; ++r)
+        if (active && r0 + r < g.Ho) xout[(r0 + r) * g.Wo + ow] = acc[r];
+      __syncwarp();
+      dwgap_finish<J>(xout, y, gap, plane, howo, lane);
+      return;
+    }
+  }
+#pragma unroll 1
+  for (int i = 0; i < 4 * J; ++i) {
+    const int f = lane + 32 * i;
+    if (f < howo) {
+      const int oh = static_cast<int>(fdiv(static_cast<uint32_t>(f), g.div_wo));
+      const int ow = f - oh * g.Wo;
+      float sum = 0.0f;
+      if (K3) {
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+          const int ih = oh * g.sh + kh - g.ph;
+          if (static_cast<unsigned>(ih) >= static_cast<unsigned>(g.H)) continue;
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw) {
+            const int iw = ow * g.sw + kw - g.pw;
+            if (static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
+              sum += xsw[ih * g.W + iw] * wk[kh * 3 + kw];
+          }
+        }
+      } else {
+        for (int kh = 0; kh < g.KH; ++kh) {
+          const int ih = oh * g.sh + kh - g.ph;
+          if (static_cast<unsigned>(ih) >= static_cast<unsigned>(g.H)) continue;
+          for (int kw = 0; kw < g.KW; ++kw) {
+            const int iw = ow * g.sw + kw - g.pw;
+            if (static_cast<unsigned>(iw) < static_cast<unsigned>(g.W))
+              sum += xsw[ih * g.W + iw] * __ldg(wc + kh * g.KW + kw);
+          }
+        }
+      }
+      if (bias) sum += bv;
+      const float t = qg * (sum - qm) * qi + qb;
+      xout[f] = kRelu ? (t < 0.0f ? 0.0f : t) : apply_act(t, act, act_alpha);  // apply_act(t, 1)
+    }
+  }
+  __syncwarp();
+  dwgap_finish<J>(xout, y, gap, plane, howo, lane);
+}
+
+
+// Input planes staged per warp: 4 for planes of up to 256 elements (several
+// HBM round trips in flight per warp), else 2.
+template <int J, int JI>
+constexpr int kDwGapStages = (J == 2 && JI == 2) ? 4 : 2;
+
+__device__ __forceinline__ void cp_async_16(void *smem_dst, const void *gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The kernel: warps take planes blockIdx.x * kDwGapWarps + warp, then every
+// gridDim.x * kDwGapWarps-th; each stages its planes in a ring of
+// kDwGapStages shared-memory blocks (plane_floats floats each: the larger of
+// the input and output planes) with 16-byte cp.async copies issued
+// kDwGapStages - 1 planes ahead, so several HBM round trips per warp overlap
+// the arithmetic of the current plane.
+template <int J, int JI, bool K3, bool kRelu, int SR = 0>
+__global__ void __launch_bounds__(kDwGapWarps * 32) dw_bn_act_gap_kernel(
+    const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ mean, const float *__restrict__ var,
+    const float *__restrict__ gamma, const float *__restrict__ beta, float eps, int act,
+    float act_alpha, float *__restrict__ y, float *__restrict__ gap, int64_t planes,
+    WindowGeom g, int plane_floats, bool uniform_channel) {
+  extern __shared__ __align__(16) float dwgap_smem[];
+  constexpr int NS = kDwGapStages<J, JI>;
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  float *ring = dwgap_smem + wib * (NS + 1) * plane_floats;  // NS staged input planes
+  float *xout = ring + NS * plane_floats;                      // activated output
+  const int hw4 = (g.H * g.W) >> 2;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kDwGapWarps;
+  int64_t plane = static_cast<int64_t>(blockIdx.x) * kDwGapWarps + wib;
+  // One commit group per plane and lane (empty past the last plane, so the
+  // group count stays the same on every lane and iteration).
+  auto issue = [&](int64_t p, int st) {
+    if (p < planes) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(x) + p * hw4;
+      float4 *dst = reinterpret_cast<float4 *>(ring + st * plane_floats);
+#pragma unroll
+      for (int j = 0; j < JI; ++j)
+        if (lane + 32 * j < hw4) cp_async_16(dst + lane + 32 * j, x4 + lane + 32 * j);
+    }
+    cp_async_commit();
+  };
+  auto channel = [&](int64_t p) {
+    const uint32_t p32 = static_cast<uint32_t>(p);
+    return static_cast<int>(p32 - fdiv(p32, g.div_c) * static_cast<uint32_t>(g.C));
+  };
+#pragma unroll
+  for (int k = 0; k < NS - 1; ++k) issue(plane + k * step, k);
+  // With step a multiple of C (the launch arranges it when it can) every
+  // plane of this warp has the first one's channel: constants loaded once.
+  DwGapConsts kc;
+  int c = plane < planes ? channel(plane) : 0;
+  dwgap_consts<K3>(kc, c, w, bias, mean, var, gamma, beta, eps);
+  int st = 0;
+  for (; plane < planes; plane += step) {
+    __syncwarp();  // every lane is done with the previous plane's stage and output block
+    issue(plane + (NS - 1) * step, st == 0 ? NS - 1 : st - 1);  // into the stage just freed
+    cp_async_wait<NS - 1>();  // this plane's copies (issued NS - 1 groups ago) have landed
+    __syncwarp();             // ... every lane's
+    const float *xsw = ring + st * plane_floats;
+    st = st + 1 == NS ? 0 : st + 1;
+    if (!uniform_channel) {
+      c = channel(plane);
+      dwgap_consts<K3>(kc, c, w, bias, mean, var, gamma, beta, eps);
+    }
+    dwgap_plane<J, K3, kRelu, SR>(xsw, xout, plane, lane, kc,
+                                  w + static_cast<int64_t>(c) * g.KH * g.KW, bias != nullptr,
+                                  act, act_alpha, y, gap, g);
+  }
+  cp_async_wait<0>();
+}
+
+template <int J, int JI, bool K3, bool kRelu, int SR = 0>
+int launch_dw_gap_one(cudaStream_t s, int grid, size_t smem, const float *x, const float *w,
+                      const float *bias, const float *mean, const float *var,
+                      const float *gamma, const float *beta, float eps, int act, float act_alpha,
+                      float *y, float *gap, int64_t planes, const WindowGeom &g, int pf) {
+  auto kernel = dw_bn_act_gap_kernel<J, JI, K3, kRelu, SR>;
+  if (smem > 48 * 1024) {
+    const int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), static_cast<int>(smem));
+    if (rc) return rc;
+  }
+  kernel<<<grid, kDwGapWarps * 32, smem, s>>>(x, w, bias, mean, var, gamma, beta, eps, act,
+                                               act_alpha, y, gap, planes, g, pf,
+                                               (static_cast<int64_t>(grid) * kDwGapWarps) % g.C == 0);
+  return kOk;
+}
+
+template <int J, int JI>
+int launch_dw_gap(cudaStream_t s, bool k3, int grid, const float *x, const float *w,
+                  const float *bias, const float *mean, const float *var, const float *gamma,
+                  const float *beta, float eps, int act, float act_alpha, float *y, float *gap,
+                  int64_t planes, const WindowGeom &g) {
+  const int pf = ((g.H * g.W > g.Ho * g.Wo ? g.H * g.W : g.Ho * g.Wo) + 3) & ~3;
+  const size_t smem =
+      static_cast<size_t>(kDwGapWarps) * (kDwGapStages<J, JI> + 1) * pf * sizeof(float);
+#define NPLK_DWGAP_ARGS s, grid, smem, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha, y, gap, planes, g, pf
+  if constexpr (J == 2 && JI == 2) {
+    // 3x3 stride 1 pad 1 on 14 x 14 / 16 x 16 planes: column strips of 7 / 8 rows
+    const bool same = k3 && g.sh == 1 && g.sw == 1 && g.ph == 1 && g.pw == 1 && g.Ho == g.H &&
+                      g.Wo == g.W;
+    const int strip_rows = same && g.W <= 32 ? (g.Ho + 32 / g.W - 1) / (32 / g.W) : 0;
+    if (strip_rows == 7 && act == 1) return launch_dw_gap_one<J, JI, true, true, 7>(NPLK_DWGAP_ARGS);
+    if (strip_rows == 8 && act == 1) return launch_dw_gap_one<J, JI, true, true, 8>(NPLK_DWGAP_ARGS);
+    if (strip_rows == 7) return launch_dw_gap_one<J, JI, true, false, 7>(NPLK_DWGAP_ARGS);
+  }
+  if (k3 && act == 1) return launch_dw_gap_one<J, JI, true, true>(NPLK_DWGAP_ARGS);
+  if (k3) return launch_dw_gap_one<J, JI, true, false>(NPLK_DWGAP_ARGS);
+  return launch_dw_gap_one<J, JI, false, false>(NPLK_DWGAP_ARGS);
+#undef NPLK_DWGAP_ARGS
+}
+
+}  // namespace nplk
+
+extern "C" int nplk_depthwise_bn_act_gap(void *stream, const nplk_conv_geom_t *g,
+                                         const float *x, const float *w, const float *bias,
+                                         const float *mean, const float *var, const float *gamma,
+                                         const float *beta, float eps, int act, float act_alpha,
+                                         float *y, float *gap) {
+  if (!g || !x || !w || !mean || !var || !gap) return kErrInvalidArg;
+  if (g->n <= 0 || g->c_in <= 0 || g->h <= 0 || g->w <= 0 || g->kh <= 0 || g->kw <= 0 ||
+      g->stride_h <= 0 || g->stride_w <= 0 || g->h_out <= 0 || g->w_out <= 0 ||
+      g->pad_top < 0 || g->pad_left < 0 || g->c_out != g->c_in)
+    return kErrInvalidArg;
+  if (act < 0 || act > 10) return kErrInvalidArg;  // nplk_activation's codes
+  const int64_t hw = g->h * g->w, howo = g->h_out * g->w_out;
+  // One plane per warp in shared memory, float4 groups on both sides.
+  if (hw > kDwGapMaxIn || hw % 4 != 0 || howo > 4 * 32 * 4 || howo % 4 != 0 ||
+      !dwgap_aligned16(x) || (y && !dwgap_aligned16(y)) ||
+      g->n * g->c_in >= (int64_t(1) << 31))
+    return kErrUnsupported;
+  WindowGeom wg{};
+  wg.C = static_cast<int>(g->c_in);
+  wg.H = static_cast<int>(g->h);
+  wg.W = static_cast<int>(g->w);
+  wg.KH = static_cast<int>(g->kh);
+  wg.KW = static_cast<int>(g->kw);
+  wg.sh = static_cast<int>(g->stride_h);
+  wg.sw = static_cast<int>(g->stride_w);
+  wg.ph = static_cast<int>(g->pad_top);
+  wg.pw = static_cast<int>(g->pad_left);
+  wg.Ho = static_cast<int>(g->h_out);
+  wg.Wo = static_cast<int>(g->w_out);
+  wg.div_wo = make_fastdiv(static_cast<uint32_t>(wg.Wo));
+  wg.div_c = make_fastdiv(static_cast<uint32_t>(wg.C));
+  const int64_t planes = g->n * g->c_in;
+  // up to 8 blocks (2048 threads) per SM; warps loop over the remaining
+  // planes. When it fits, the warp count is a multiple of C, so that each
+  // warp's planes share one channel (its constants are loaded once).
+  const int64_t want = ceil_div(planes, kDwGapWarps), cap = static_cast<int64_t>(sm_count()) * 8;
+  int64_t grid64 = want < cap ? want : cap;
+  const int64_t unit = g->c_in / std::gcd(g->c_in, static_cast<int64_t>(kDwGapWarps));
+  if (grid64 < want && unit <= cap) grid64 = cap / unit * unit;
+  const int grid = static_cast<int>(grid64);
+  const bool k3 = g->kh == 3 && g->kw == 3;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int j = howo <= 256 ? 2 : 4;
+  const int ji = hw <= 256 ? 2 : (hw <= 512 ? 4 : 8);
+  int rc;
+  if (j == 2 && ji == 2)
+    rc = launch_dw_gap<2, 2>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
+                             y, gap, planes, wg);
+  else if (j == 2 && ji == 4)
+    rc = launch_dw_gap<2, 4>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
+                             y, gap, planes, wg);
+  else if (j == 2)
+    rc = launch_dw_gap<2, 8>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
+                             y, gap, planes, wg);
+  else if (ji <= 4)
+    rc = launch_dw_gap<4, 4>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
+                             y, gap, planes, wg);
+  else
+    rc = launch_dw_gap<4, 8>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
+                             y, gap, planes, wg);
+  if (rc) return rc;
+  count_launch();
+  return launch_result();
+}
 
 extern "C" int nplk_depthwise_conv2d(void *stream, const nplk_conv_geom_t *g, const float *x,
                                      const float *w, const float *bias, float *out) {

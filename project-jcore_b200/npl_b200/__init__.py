@@ -188,6 +188,8 @@ NPLK_SIGNATURES = {
     "nplk_conv2d_maxpool_fused": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
                                             C.c_int, _F, _VP, _VP, C.c_size_t, _VP]),
     "nplk_depthwise_conv2d": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP]),
+    "nplk_depthwise_bn_act_gap": (C.c_int, [_VP, _G, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _F,
+                                            C.c_int, _F, _VP, _VP]),
     "nplk_batch_norm_infer": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _VP, _F]),
     "nplk_batch_norm_stats": (C.c_int, [_VP, _I64, _I64, _I64, _VP, _VP, _VP]),
     "nplk_bn_update_running": (C.c_int, [_VP, _I64, _VP, _VP, _VP, _VP, _F]),

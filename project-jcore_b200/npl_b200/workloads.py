@@ -42,6 +42,25 @@ def bandwidth_chain(lib, stream, x, w, mean, var, gamma, beta, dw_out, act_out, 
     return next((r for r in rcs if r != 0), 0)
 
 
+def bandwidth_chain_fused(lib, stream, x, w, mean, var, gamma, beta, gap, probs,
+                          act_out=None, eps: float = 1e-5) -> int:
+    """The same chain with its first four calls in one pass
+    (nplk_depthwise_bn_act_gap: depthwise, BN, ReLU and the average pool
+    without writing the intermediate maps; act_out, when given, receives the
+    ReLU(BN(.)) map), then the softmax over the channels. gap and probs equal
+    bandwidth_chain's bit for bit."""
+    from . import conv_geom
+
+    n, c, h, wd = x.shape
+    g = conv_geom(n, c, h, wd, c, 3, 3, 1, 1)
+    rc = lib.nplk_depthwise_bn_act_gap(stream, C.byref(g), _p(x), _p(w), None, _p(mean),
+                                       _p(var), _p(gamma), _p(beta), eps, 1, 0.0,
+                                       _p(act_out) if act_out is not None else None, _p(gap))
+    if rc != 0:
+        return rc
+    return lib.nplk_softmax(stream, n, c, 1, _p(gap), _p(probs))
+
+
 def gemm_bias_relu_layer_norm(lib, stream, A, B, Cm, Y, work, ws: int, eps: float = 1e-5,
                               flags: int = 0, between=None) -> int:
     """The large-GEMM workload after its bias fill: Cm = ReLU(A @ B + Cm) with

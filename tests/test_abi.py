@@ -131,6 +131,23 @@ def test_kernel_abi_argument_checks(lib):
     assert lib.nplk_softmax(None, 0, 4, 1, None, None) == nb.NPL_ERR_INVALID_ARG
     assert lib.nplk_pool2d(None, 1, 1, 4, 4, 2, 2, 2, 2, 0, 0, 2, 2, 5, 0, None, None) == \
         nb.NPL_ERR_INVALID_ARG
+    # fused depthwise -> BN -> activation -> average pool: missing tensors, a
+    # c_out that differs from c_in, an unknown activation
+    gd = nb.conv_geom(2, 4, 8, 8, 4, 3, 3, 1, 1)
+    fake = C.c_void_p(256)  # never dereferenced: the checks come first
+    assert lib.nplk_depthwise_bn_act_gap(None, C.byref(gd), None, fake, None, fake, fake, None,
+                                         None, 1e-5, 1, 0.0, None, fake) == nb.NPL_ERR_INVALID_ARG
+    gbad = nb.conv_geom(2, 4, 8, 8, 5, 3, 3, 1, 1)
+    assert lib.nplk_depthwise_bn_act_gap(None, C.byref(gbad), fake, fake, None, fake, fake,
+                                         None, None, 1e-5, 1, 0.0, None, fake) == \
+        nb.NPL_ERR_INVALID_ARG
+    assert lib.nplk_depthwise_bn_act_gap(None, C.byref(gd), fake, fake, None, fake, fake, None,
+                                         None, 1e-5, 11, 0.0, None, fake) == nb.NPL_ERR_INVALID_ARG
+    # planes the one-pass form does not take (output plane of 7x7 = 49, not a
+    # multiple of 4) are refused before any device work
+    g7 = nb.conv_geom(2, 4, 7, 7, 4, 3, 3, 1, 1)
+    assert lib.nplk_depthwise_bn_act_gap(None, C.byref(g7), fake, fake, None, fake, fake, None,
+                                         None, 1e-5, 1, 0.0, None, fake) == nb.NPL_ERR_UNSUPPORTED
 
 
 def test_multi_gpu_entry_points_argument_checks(lib):
