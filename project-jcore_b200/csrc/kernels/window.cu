@@ -843,6 +843,189 @@ __global__ void __launch_bounds__(kDwGapWarps * 32) dw_bn_act_gap_kernel(
   cp_async_wait<0>();
 }
 
+// Same-size 3x3 stride-1 pad-1 planes of R x R (R = 14 or 16): a warp takes
+// four planes of one channel at a time (images 4k .. 4k+3), R / 2 lanes per
+// plane, each lane two adjacent output columns down the whole plane: every
+// input row's four columns are read once and folded into the output rows they
+// feed in kh order (kw order within a row), so each output gets the depthwise
+// kernel's sum term by term, padding entering as zero products (exact for
+// finite weights; a channel with a non-finite weight takes the per-output
+// form). About a third of the per-output path's instructions per plane.
+constexpr int kDwQuadWarps = 4;   // warps per block
+constexpr int kDwQuadStages = 2;  // staged quads per warp
+
+template <int R>
+__device__ __forceinline__ void dwquad_plane_slow(const float *xs, float *xo, int lane,
+                                                  const DwGapConsts &kc, bool has_bias,
+                                                  int act, float act_alpha) {
+  constexpr int HW = R * R;
+#pragma unroll 1
+  for (int f = lane; f < HW; f += 32) {
+    const int oh = f / R, ow = f - (f / R) * R;
+    float sum = 0.0f;
+    for (int kh = 0; kh < 3; ++kh) {
+      const int ih = oh + kh - 1;
+      if (static_cast<unsigned>(ih) >= static_cast<unsigned>(R)) continue;
+      for (int kw = 0; kw < 3; ++kw) {
+        const int iw = ow + kw - 1;
+        if (static_cast<unsigned>(iw) < static_cast<unsigned>(R))
+          sum += xs[ih * R + iw] * kc.wk[kh * 3 + kw];
+      }
+    }
+    if (has_bias) sum += kc.bv;
+    xo[f] = apply_act(kc.qg * (sum - kc.qm) * kc.qi + kc.qb, act, act_alpha);
+  }
+}
+
+template <int R, bool kRelu>
+__global__ void __launch_bounds__(kDwQuadWarps * 32) dw_bn_act_gap_quad_kernel(
+    const float *__restrict__ x, const float *__restrict__ w, const float *__restrict__ bias,
+    const float *__restrict__ mean, const float *__restrict__ var,
+    const float *__restrict__ gamma, const float *__restrict__ beta, float eps, int act,
+    float act_alpha, float *__restrict__ y, float *__restrict__ gap, int64_t n_img, int C,
+    FastDiv div_c, bool uniform_channel) {
+  constexpr int HW = R * R, HW4 = HW / 4, QPL = R / 2, NS = kDwQuadStages;
+  constexpr int kChunks = 4 * HW4, kChunksPerLane = (kChunks + 31) / 32;
+  extern __shared__ __align__(16) float dwquad_smem[];
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  float *ring = dwquad_smem + wib * (NS + 1) * 4 * HW;  // NS stages of four planes
+  float *xout = ring + NS * 4 * HW;                     // the four activated planes
+  const int64_t groups = (n_img + 3) / 4;
+  const int64_t quads = groups * C;
+  const int64_t step = static_cast<int64_t>(gridDim.x) * kDwQuadWarps;
+  int64_t q = static_cast<int64_t>(blockIdx.x) * kDwQuadWarps + wib;
+  // quads < 2^31 (the entry point bounds N * C): 32-bit quotient and remainder
+  auto chan = [&](int64_t qq) {
+    const uint32_t q32 = static_cast<uint32_t>(qq);
+    return static_cast<int>(q32 - fdiv(q32, div_c) * static_cast<uint32_t>(C));
+  };
+  auto group0 = [&](int64_t qq) {
+    return static_cast<int64_t>(fdiv(static_cast<uint32_t>(qq), div_c)) * 4;
+  };
+  auto issue = [&](int64_t qq, int st) {
+    if (qq < quads) {
+      const int c = chan(qq);
+      const int64_t n0 = group0(qq);
+      float *dst = ring + st * 4 * HW;
+#pragma unroll
+      for (int j = 0; j < kChunksPerLane; ++j) {
+        const int k = lane + 32 * j;
+        const int i = k / HW4, off = k - (k / HW4) * HW4;
+        if (k < kChunks && n0 + i < n_img)
+          cp_async_16(dst + i * HW + 4 * off,
+                      x + ((n0 + i) * C + c) * static_cast<int64_t>(HW) + 4 * off);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < NS - 1; ++k) issue(q + k * step, k);
+  DwGapConsts kc;
+  int c = q < quads ? chan(q) : 0;
+  dwgap_consts<true>(kc, c, w, bias, mean, var, gamma, beta, eps);
+  const int pl = lane / QPL, col0 = 2 * (lane - pl * QPL);
+  int st = 0;
+  for (; q < quads; q += step) {
+    __syncwarp();  // every lane is done with the previous quad's stage and output blocks
+    issue(q + (NS - 1) * step, st == 0 ? NS - 1 : st - 1);
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+    const float *xs = ring + st * 4 * HW;
+    st = st + 1 == NS ? 0 : st + 1;
+    if (!uniform_channel) {
+      c = chan(q);
+      dwgap_consts<true>(kc, c, w, bias, mean, var, gamma, beta, eps);
+    }
+    const int64_t n0 = group0(q);
+    bool finite = true;
+#pragma unroll
+    for (int t = 0; t < 9; ++t) finite = finite && isfinite(kc.wk[t]);
+    if (finite) {
+      const bool active = pl < 4 && n0 + pl < n_img;
+      const float *xp = xs + (pl < 4 ? pl : 0) * HW;
+      float acc[R][2];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r][0] = acc[r][1] = 0.0f;
+#pragma unroll
+      for (int t = 0; t < R + 2; ++t) {  // input rows -1 .. R
+        const int ih = t - 1;
+        const bool rin = active && ih >= 0 && ih < R;
+        // indices clamped into the plane, so no address leaves it
+        const int base = (rin ? ih : 0) * R + col0;
+        const float v0 = (rin && col0 > 0) ? xp[base - (col0 > 0 ? 1 : 0)] : 0.0f;
+        const float v1 = rin ? xp[base] : 0.0f;
+        const float v2 = rin ? xp[base + 1] : 0.0f;
+        const float v3 = (rin && col0 + 2 < R) ? xp[base + (col0 + 2 < R ? 2 : 1)] : 0.0f;
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh) {
+          const int r = t - kh;  // output row r takes input row ih as its tap row kh
+          if (r >= 0 && r < R) {
+            acc[r][0] += v0 * kc.wk[kh * 3 + 0];
+            acc[r][0] += v1 * kc.wk[kh * 3 + 1];
+            acc[r][0] += v2 * kc.wk[kh * 3 + 2];
+            acc[r][1] += v1 * kc.wk[kh * 3 + 0];
+            acc[r][1] += v2 * kc.wk[kh * 3 + 1];
+            acc[r][1] += v3 * kc.wk[kh * 3 + 2];
+          }
+        }
+      }
+      if (active) {
+        float *xo = xout + pl * HW + col0;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float o[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float sum = acc[r][e];
+            if (bias) sum += kc.bv;
+            const float t = kc.qg * (sum - kc.qm) * kc.qi + kc.qb;
+            o[e] = kRelu ? (t < 0.0f ? 0.0f : t) : apply_act(t, act, act_alpha);
+          }
+          *reinterpret_cast<float2 *>(xo + r * R) = make_float2(o[0], o[1]);
+        }
+      }
+    } else {
+      for (int i = 0; i < 4; ++i)
+        if (n0 + i < n_img)
+          dwquad_plane_slow<R>(xs + i * HW, xout + i * HW, lane, kc, bias != nullptr, act,
+                               act_alpha);
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {
+      const int64_t n = n0 + i;
+      if (n >= n_img) break;
+      dwgap_finish<(HW4 + 31) / 32>(xout + i * HW, y, gap, n * C + c, HW, lane);
+    }
+  }
+  cp_async_wait<0>();
+}
+
+template <int R, bool kRelu>
+int launch_dw_quad(cudaStream_t s, const float *x, const float *w, const float *bias,
+                   const float *mean, const float *var, const float *gamma, const float *beta,
+                   float eps, int act, float act_alpha, float *y, float *gap, int64_t n_img,
+                   int C) {
+  auto kernel = dw_bn_act_gap_quad_kernel<R, kRelu>;
+  const size_t smem =
+      static_cast<size_t>(kDwQuadWarps) * (kDwQuadStages + 1) * 4 * R * R * sizeof(float);
+  const int rc = ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), static_cast<int>(smem));
+  if (rc) return rc;
+  // Up to 6 blocks per SM (shared memory: 37.6 KB per block for 14 x 14); when
+  // it fits, a warp count that is a multiple of C
+  // (each warp then keeps one channel's constants).
+  const int64_t quads = (n_img + 3) / 4 * C;
+  const int64_t want = ceil_div(quads, kDwQuadWarps), cap = static_cast<int64_t>(sm_count()) * 6;
+  int64_t grid = want < cap ? want : cap;
+  const int64_t unit = C / std::gcd(static_cast<int64_t>(C), static_cast<int64_t>(kDwQuadWarps));
+  if (grid < want && unit <= cap) grid = cap / unit * unit;
+  kernel<<<static_cast<int>(grid), kDwQuadWarps * 32, smem, s>>>(
+      x, w, bias, mean, var, gamma, beta, eps, act, act_alpha, y, gap, n_img, C,
+      make_fastdiv(static_cast<uint32_t>(C)), (grid * kDwQuadWarps) % C == 0);
+  return kOk;
+}
+
 template <int J, int JI, bool K3, bool kRelu, int SR = 0>
 int launch_dw_gap_one(cudaStream_t s, int grid, size_t smem, const float *x, const float *w,
                       const float *bias, const float *mean, const float *var,
@@ -930,7 +1113,20 @@ extern "C" int nplk_depthwise_bn_act_gap(void *stream, const nplk_conv_geom_t *g
   const int j = howo <= 256 ? 2 : 4;
   const int ji = hw <= 256 ? 2 : (hw <= 512 ? 4 : 8);
   int rc;
-  if (j == 2 && ji == 2)
+  const bool quad = k3 && g->stride_h == 1 && g->stride_w == 1 && g->pad_top == 1 &&
+                    g->pad_left == 1 && g->h == g->w && g->h_out == g->h && g->w_out == g->w &&
+                    (g->h == 14 || g->h == 16) && wg.C < (1 << 20);
+  if (quad && g->h == 14)
+    rc = act == 1 ? launch_dw_quad<14, true>(s, x, w, bias, mean, var, gamma, beta, eps, act,
+                                             act_alpha, y, gap, g->n, wg.C)
+                  : launch_dw_quad<14, false>(s, x, w, bias, mean, var, gamma, beta, eps, act,
+                                              act_alpha, y, gap, g->n, wg.C);
+  else if (quad)
+    rc = act == 1 ? launch_dw_quad<16, true>(s, x, w, bias, mean, var, gamma, beta, eps, act,
+                                             act_alpha, y, gap, g->n, wg.C)
+                  : launch_dw_quad<16, false>(s, x, w, bias, mean, var, gamma, beta, eps, act,
+                                              act_alpha, y, gap, g->n, wg.C);
+  else if (j == 2 && ji == 2)
     rc = launch_dw_gap<2, 2>(s, k3, grid, x, w, bias, mean, var, gamma, beta, eps, act, act_alpha,
                              y, gap, planes, wg);
   else if (j == 2 && ji == 4)

@@ -9,6 +9,7 @@ and checks the kernel status word.
     python -m npl_b200.profile_cases stem      # 7x7/s2 conv+BN+ReLU, N=16 3->64 224x224
     python -m npl_b200.profile_cases gemm      # 4096x4096x8192 3xTF32 GEMM
     python -m npl_b200.profile_cases chain     # depthwise, BN, ReLU, GAP, softmax 256x512x14x14
+    python -m npl_b200.profile_cases chain_fused # the same chain, its first four calls in one pass
     python -m npl_b200.profile_cases layernorm # 8192 x 16384 rows
     python -m npl_b200.profile_cases pool      # max pool 3x3/s2 [32,64,112,112] -> 56x56
     python -m npl_b200.profile_cases gemm_raw  # the 4096x4096x8192 GEMM, raw operand form
@@ -103,6 +104,24 @@ def case_chain(reps: int = 3):
         assert lib.nplk_global_avg_pool(s, n * c, hw * hw, _p(t2), _p(gap)) == 0
         assert lib.nplk_softmax(s, n, c, 1, _p(gap), _p(sm)) == 0
     torch.cuda.synchronize()
+
+
+def case_chain_fused(reps: int = 3):
+    """The bandwidth chain's fused pass (nplk_depthwise_bn_act_gap, no map
+    written) and its softmax on [256,512,14,14]."""
+    from . import workloads
+    torch, lib, s = _setup()
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    n, c, hw = 256, 512, 14
+    x = torch.randn(n, c, hw, hw, device="cuda", generator=gen)
+    w = torch.randn(c, 1, 3, 3, device="cuda", generator=gen) * 0.3
+    bn = [torch.rand(c, device="cuda", generator=gen) + 0.5 for _ in range(4)]
+    gap, sm = torch.empty(n, c, device="cuda"), torch.empty(n, c, device="cuda")
+    for _ in range(reps):
+        assert workloads.bandwidth_chain_fused(lib, s, x, w, bn[0], bn[1], bn[2], bn[3], gap,
+                                               sm) == 0
+    torch.cuda.synchronize()
+    assert lib.nplk_read_status(s) == 0
 
 
 def case_pool(reps: int = 3):
@@ -204,7 +223,7 @@ def case_stem_fused(reps: int = 2, n: int = 16):
     assert torch.equal(fused, pooled)
 
 
-CASES = {"conv": case_conv,
+CASES = {"conv": case_conv, "chain_fused": case_chain_fused,
          "conv_direct": lambda: case_conv(algo=1),
          "conv_window_tma": lambda: case_conv(algo=3),
          "conv_s2": lambda: case_conv(cout=128, stride=2),
