@@ -560,9 +560,11 @@ def run_b200(args, rank, world, local_rank):
     ms_per_step, conv_kernel_ms = stats.tolist()
 
     # ---- e2e through the public C ABI with pinned host buffers ----
-    # With several ranks, each process first moves to its GPU's local CPUs so
-    # its pinned buffers sit on that socket.
-    cpus_bound = bind_host_to_gpu(local_rank) if world > 1 else None
+    # The process first moves to its GPU's local CPUs so its pinned buffers
+    # sit on that socket; the affinity is restored after this leg (the CPU
+    # baseline below uses every host thread).
+    saved_affinity = os.sched_getaffinity(0)
+    cpus_bound = bind_host_to_gpu(local_rank)
     hx = torch.from_numpy(x).pin_memory()
     hw_ = torch.from_numpy(w).pin_memory()
     hy = torch.empty((N_IMG, C_OUT, HW_IN, HW_IN)).pin_memory()
@@ -617,6 +619,7 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(link_s, op=dist.ReduceOp.MAX)
     link_step = float(link_s.item())
     del dx, dy
+    os.sched_setaffinity(0, saved_affinity)
 
     result = None
     if rank == 0:
