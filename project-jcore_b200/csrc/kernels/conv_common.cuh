@@ -39,7 +39,38 @@ struct ConvParams {
   float act_alpha;
   uint32_t stall_us;  // fault injection: 0 except on an armed launch (injected_stall)
   int *status;
+  // 2-D tiles (direct kernel, row order): t2d_w > 0 makes each GEMM tile
+  // t2d_w output columns x (128 / t2d_w) output rows of one image (t2d_cols
+  // tiles across an output row, t2d_tiles per image) instead of 128
+  // consecutive pixels, so one tile's input rows stay few and L1-resident.
+  int t2d_w, t2d_cols, t2d_tiles;
 };
+
+// GEMM row r (0..127) of tile mb as an output pixel (n, oh, ow): 1-D tiles
+// take 128 consecutive pixels in (n, oh, ow) order (GEMM rows are real
+// pixels: Wv == Wo), 2-D tiles their block of one image. False past the last
+// pixel (n, oh, ow are then 0).
+__device__ __forceinline__ bool conv_tile_pixel(const ConvParams &p, int mb, int r, int &n,
+                                                int &oh, int &ow) {
+  if (p.t2d_w == 0) {
+    const int m = mb * kConvBM + r;
+    n = oh = ow = 0;
+    if (m >= p.M) return false;
+    n = m / static_cast<int>(p.HoWo);
+    const int pix = m - n * static_cast<int>(p.HoWo);
+    oh = pix / p.Wo;
+    ow = pix - oh * p.Wo;
+    return true;
+  }
+  n = mb / p.t2d_tiles;
+  const int t = mb - n * p.t2d_tiles;
+  const int tr = t / p.t2d_cols;
+  const int tc = t - tr * p.t2d_cols;
+  const int dy = r / p.t2d_w;
+  oh = tr * (kConvBM / p.t2d_w) + dy;
+  ow = tc * p.t2d_w + (r - dy * p.t2d_w);
+  return true;
+}
 
 // Epilogue activation selected at compile time for the common cases.
 enum { kEpiActNone = 0, kEpiActRelu = 1, kEpiActAny = 2 };
@@ -119,7 +150,11 @@ __device__ __forceinline__ bool conv_epilogue_tile(const ConvParams &p, uint32_t
   const int m = mb * kConvBM + quad * 32 + lane;  // GEMM row (virtual pixel)
   bool valid = m < p.Mv;
   int n = 0, pix = 0;
-  if (valid) {
+  if (p.t2d_w) {
+    int oh, ow;
+    valid = conv_tile_pixel(p, mb, quad * 32 + lane, n, oh, ow);
+    pix = oh * p.Wo + ow;
+  } else if (valid) {
     const int howv = p.Ho * p.Wv;
     n = m / howv;
     const int rem = m - n * howv;

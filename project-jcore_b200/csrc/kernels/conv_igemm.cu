@@ -158,15 +158,8 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
         nb = tile - mb * p.n_blocks;
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          const int m = mb * kConvBM + gt + 64 * r;
-          valid[r] = m < p.M;
-          int n = 0, oh = 0, ow = 0;
-          if (valid[r]) {
-            n = m / static_cast<int>(p.HoWo);
-            const int pix = m - n * static_cast<int>(p.HoWo);
-            oh = pix / p.Wo;
-            ow = pix - oh * p.Wo;
-          }
+          int n, oh, ow;
+          valid[r] = conv_tile_pixel(p, mb, gt + 64 * r, n, oh, ow);
           ih0[r] = oh * p.sh - p.pt;
           iw0[r] = ow * p.sw - p.pl;
           xb[r] = p.x + static_cast<int64_t>(n) * p.CHW;
@@ -599,7 +592,18 @@ int dispatch_mode(cudaStream_t s, const ConvPlan &c, const float *wsplit, const 
   }
 }
 
-int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, const ConvParams &prm) {
+int dispatch_conv(cudaStream_t s, const ConvPlan &c, const float *wsplit, ConvParams prm) {
+  // Row order (C_in not a multiple of 32: the stem's 3 channels) with output
+  // planes of whole 16 x 8 blocks: 2-D tiles. A 1-D tile spans ~1.1 output
+  // rows and gathers 7-9 whole input rows per channel, whose vertical reuse
+  // falls in other tiles; a 16 x 8 tile of a 7x7 stride-2 filter gathers a
+  // 21 x 37 patch per channel (a third of the lines), reused inside the tile.
+  if ((c.mode == 4 || c.mode == 8) && prm.Wo % 16 == 0 && prm.Ho % 8 == 0) {
+    prm.t2d_w = 16;
+    prm.t2d_cols = prm.Wo / 16;
+    prm.t2d_tiles = (prm.Ho / 8) * prm.t2d_cols;
+    prm.m_blocks = static_cast<int>(static_cast<int64_t>(prm.M) / kConvBM);
+  }
   return c.bnc == 64 ? dispatch_mode<64>(s, c, wsplit, prm) : dispatch_mode<128>(s, c, wsplit, prm);
 }
 

@@ -127,6 +127,8 @@ def test_stem_conv_bn_relu_then_maxpool():
     (1, 12, 15, 16, 33, (4, 4), (2, 2), (1, 1), (1, 1)),    # row order, 4 slots all used
     (2, 7, 19, 23, 40, (2, 6), (1, 2), (0, 2), (1, 1)),     # row order, 8 slots, KH != KW
     (2, 6, 20, 18, 16, (3, 5), (1, 1), (2, 2), (2, 1)),     # row order with vertical dilation
+    (2, 16, 32, 32, 130, (3, 3), (1, 1), (1, 1), (1, 1)),   # row order, 16 x 8 tiles, two Cout blocks
+    (3, 3, 64, 64, 64, (7, 7), (2, 2), (3, 3), (1, 1)),     # stem-like, 16 x 8 tiles over 3 images
 ])
 def test_conv2d_shapes(n, cin, h, w, cout, k, stride, pad, dil):
     lib = S.gpu_lib()
