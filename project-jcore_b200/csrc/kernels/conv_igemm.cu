@@ -377,6 +377,10 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
                                  int64_t wsplit_elems, const float *bias, const float *mean,
                                  const float *var, const float *gamma, const float *beta,
                                  float eps, float *__restrict__ ep, int cout_pad) {
+  // The conv kernel that follows in nplk_conv2d_fused may be scheduled now
+  // and start gathering x; its weight and constant readers wait
+  // (griddep_wait) for this grid to complete and its writes to be visible.
+  griddep_launch_dependents();
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const int K = C * KH * KW;
@@ -428,9 +432,6 @@ __global__ void conv_prep_kernel(const float *__restrict__ w, int Cout, int C, i
     ep[kEpBeta * cout_pad + c] = (in && beta) ? beta[c] : 0.0f;
     ep[kEpInvStd * cout_pad + c] = (in && var) ? 1.0f / sqrtf(var[c] + eps) : 1.0f;
   }
-  // The conv kernel that follows in nplk_conv2d_fused may start now; it
-  // waits (griddep_wait) before reading what this kernel wrote.
-  griddep_launch_dependents();
 }
 
 namespace {
