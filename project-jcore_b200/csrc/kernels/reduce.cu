@@ -45,6 +45,10 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 template <int NV>
 __global__ void softmax_rows_warp_kernel(const float *__restrict__ x, float *__restrict__ y,
                                          int64_t rows, int cols) {
+  // Launched as a programmatic dependent: the kernel before it (when it
+  // allows an early launch) has completed and its writes are visible past
+  // this wait; after any other kernel it returns at once.
+  griddep_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
@@ -89,6 +93,7 @@ __global__ void softmax_rows_warp_kernel(const float *__restrict__ x, float *__r
 // axis; consecutive threads take consecutive inner indices (coalesced).
 __global__ void softmax_strided_kernel(const float *__restrict__ x, float *__restrict__ y,
                                        int64_t outer, int64_t axis_len, int64_t inner) {
+  griddep_wait();  // as in softmax_rows_warp_kernel
   const int64_t lines = outer * inner;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t l = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; l < lines;
@@ -367,22 +372,22 @@ __global__ void gap_kernel(const float *__restrict__ x, float *__restrict__ y, i
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   if constexpr (J > 0) {
     gap_planes<J>(x, y, planes, hw, static_cast<int>(hw / 4), warp_id, nwarps, lane);
-    return;
-  }
-  for (int64_t p = warp_id; p < planes; p += nwarps) {
-    const float *xp = x + p * hw;
-    float s = 0.0f;
-    if (vec) {
-      const float4 *x4 = reinterpret_cast<const float4 *>(xp);
-      for (int64_t j = lane; j < hw / 4; j += 32) {
-        const float4 v = x4[j];
-        s += (v.x + v.y) + (v.z + v.w);
+  } else {
+    for (int64_t p = warp_id; p < planes; p += nwarps) {
+      const float *xp = x + p * hw;
+      float s = 0.0f;
+      if (vec) {
+        const float4 *x4 = reinterpret_cast<const float4 *>(xp);
+        for (int64_t j = lane; j < hw / 4; j += 32) {
+          const float4 v = x4[j];
+          s += (v.x + v.y) + (v.z + v.w);
+        }
+      } else {
+        for (int64_t j = lane; j < hw; j += 32) s += xp[j];
       }
-    } else {
-      for (int64_t j = lane; j < hw; j += 32) s += xp[j];
+      s = warp_sum(s);
+      if (lane == 0) y[p] = s / static_cast<float>(hw);
     }
-    s = warp_sum(s);
-    if (lane == 0) y[p] = s / static_cast<float>(hw);
   }
 }
 
@@ -474,18 +479,20 @@ extern "C" int nplk_softmax(void *stream, int64_t outer, int64_t axis_len, int64
     const int64_t blocks = ceil_div(outer, static_cast<int64_t>(threads / 32));
     const int grid = static_cast<int>(blocks < (int64_t(1) << 30) ? blocks : (int64_t(1) << 30));
     const int cols = static_cast<int>(axis_len);
+    // Programmatic launches (the kernels wait for their predecessor first):
+    // behind a kernel that allows it -- the bandwidth chain's one-pass kernel
+    // -- the softmax's launch overlaps that kernel's last wave.
     if (c4 <= 32 * 4)
-      softmax_rows_warp_kernel<4><<<grid, threads, 0, s>>>(x, y, outer, cols);
-    else if (c4 <= 32 * 8)
-      softmax_rows_warp_kernel<8><<<grid, threads, 0, s>>>(x, y, outer, cols);
-    else
-      softmax_rows_warp_kernel<16><<<grid, threads, 0, s>>>(x, y, outer, cols);
-  } else {
-    softmax_strided_kernel<<<grid_for(outer * inner, 256), 256, 0, s>>>(x, y, outer, axis_len,
-                                                                       inner);
+      return launch_programmatic(softmax_rows_warp_kernel<4>, dim3(grid), dim3(threads), 0, s, x,
+                                 y, outer, cols);
+    if (c4 <= 32 * 8)
+      return launch_programmatic(softmax_rows_warp_kernel<8>, dim3(grid), dim3(threads), 0, s, x,
+                                 y, outer, cols);
+    return launch_programmatic(softmax_rows_warp_kernel<16>, dim3(grid), dim3(threads), 0, s, x, y,
+                               outer, cols);
   }
-  count_launch();
-  return launch_result();
+  return launch_programmatic(softmax_strided_kernel, dim3(grid_for(outer * inner, 256)), dim3(256),
+                             0, s, x, y, outer, axis_len, inner);
 }
 
 extern "C" int nplk_layer_norm(void *stream, int64_t rows, int64_t cols, const float *x,

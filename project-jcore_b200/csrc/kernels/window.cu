@@ -793,6 +793,9 @@ __global__ void __launch_bounds__(kDwGapWarps * 32) dw_bn_act_gap_kernel(
     float act_alpha, float *__restrict__ y, float *__restrict__ gap, int64_t planes,
     WindowGeom g, int plane_floats, bool uniform_channel) {
   extern __shared__ __align__(16) float dwgap_smem[];
+  // The softmax that follows in the chain may be scheduled now; it waits for
+  // this grid's completion before reading the pooled values.
+  griddep_launch_dependents();
   constexpr int NS = kDwGapStages<J, JI>;
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -887,6 +890,7 @@ __global__ void __launch_bounds__(kDwQuadWarps * 32) dw_bn_act_gap_quad_kernel(
   constexpr int HW = R * R, HW4 = HW / 4, QPL = R / 2, NS = kDwQuadStages;
   constexpr int kChunks = 4 * HW4, kChunksPerLane = (kChunks + 31) / 32;
   extern __shared__ __align__(16) float dwquad_smem[];
+  griddep_launch_dependents();  // as in dw_bn_act_gap_kernel
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   float *ring = dwquad_smem + wib * (NS + 1) * 4 * HW;  // NS stages of four planes
