@@ -276,11 +276,17 @@ __global__ void __launch_bounds__(ConvTraits<BNC>::kThreads, 1)
         const int row = gt + 64 * r;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          float4 hi, lo;
-          tf32_split_trunc(v[r][4 * c + 0], hi.x, lo.x);
-          tf32_split_trunc(v[r][4 * c + 1], hi.y, lo.y);
-          tf32_split_trunc(v[r][4 * c + 2], hi.z, lo.z);
-          tf32_split_trunc(v[r][4 * c + 3], hi.w, lo.w);
+          // The hi part is stored as the raw value: the tensor core reads a
+          // tf32 operand as the truncation of its fp32 bits, which is
+          // exactly tf32_split_trunc's hi.
+          const float4 hi = make_float4(v[r][4 * c + 0], v[r][4 * c + 1], v[r][4 * c + 2],
+                                        v[r][4 * c + 3]);
+          float4 lo;
+          float t;
+          tf32_split_trunc(hi.x, t, lo.x);
+          tf32_split_trunc(hi.y, t, lo.y);
+          tf32_split_trunc(hi.z, t, lo.z);
+          tf32_split_trunc(hi.w, t, lo.w);
           const uint32_t off = sw128_offset(row, c);
           *reinterpret_cast<float4 *>(a_hi + off) = hi;
           *reinterpret_cast<float4 *>(a_lo + off) = lo;
