@@ -1202,9 +1202,10 @@ def gemm_dist(args, rank, world, local_rank):
     full_f = torch.empty(GEMM_M, GEMM_N, device=dev)
     peers = nd.PeerBuffers(full_f, world, rank)
 
-    def fused_ms(flags):
+    def fused_ms(flags, dst=None):
+        dst = peers if dst is None else dst
         for _ in range(2):
-            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work, flags=flags)
+            nd.column_sharded_gemm_fused(A, B, dst, bias, workspace=work, flags=flags)
         torch.cuda.synchronize()
         dist.barrier()
         f_ms = []
@@ -1212,7 +1213,7 @@ def gemm_dist(args, rank, world, local_rank):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            nd.column_sharded_gemm_fused(A, B, peers, bias, workspace=work, flags=flags)
+            nd.column_sharded_gemm_fused(A, B, dst, bias, workspace=work, flags=flags)
             e1.record(stream)
             torch.cuda.synchronize()
             dist.barrier()
@@ -1227,6 +1228,23 @@ def gemm_dist(args, rank, world, local_rank):
         ferr = ((full_f[rows].double() - ref).abs().max() / ref.abs().max()).item()
     finally:
         peers.close()
+    # Multicast form: every rank's C bound to one NVLink multicast object; the
+    # epilogue stores each tile once and NVSwitch delivers it to all ranks.
+    mc, mc_ms, mc_why = None, None, None
+    if os.environ.get("NPL_BENCH_NO_MULTICAST", "0") != "1":
+        try:
+            mc = nd.MulticastBuffers((GEMM_M, GEMM_N), world, rank)
+        except RuntimeError as e:
+            mc_why = str(e)[:200]
+    else:
+        mc_why = "skipped (NPL_BENCH_NO_MULTICAST=1)"
+    if mc is not None:
+        try:
+            mc_ms = fused_ms(0, mc)
+            full_mc = mc.tensor.clone()
+        finally:
+            mc.close()
+        mc = None
     # Every rank's whole C against a one-GPU GEMM of the same inputs on this
     # rank (same k order and epilogue, so bit-identical is expected), for
     # both exchange forms.
@@ -1239,7 +1257,8 @@ def gemm_dist(args, rank, world, local_rank):
                       0, C.c_void_p(work_full.data_ptr()), ws_full, None)
     assert r == 0, r
     torch.cuda.synchronize()
-    same = torch.tensor([int(torch.equal(full_f, c_ref)), int(torch.equal(full, c_ref))],
+    same = torch.tensor([int(torch.equal(full_f, c_ref)), int(torch.equal(full, c_ref)),
+                         int(torch.equal(full_mc, c_ref)) if mc_ms is not None else 1],
                         device=dev, dtype=torch.int64)
     diff = torch.tensor([((full_f - c_ref).abs().max() / c_ref.abs().max()).item()],
                         device=dev, dtype=torch.float64)
@@ -1248,11 +1267,28 @@ def gemm_dist(args, rank, world, local_rank):
     del work_full, c_ref
     torch.cuda.empty_cache()
     egress = (world - 1) * GEMM_M * (GEMM_N // world) * 4  # bytes each rank stores to peers
+    if mc_ms is not None:
+        multimem = {"ms": round(mc_ms, 4), "value": round(GEMM_FLOPS / (mc_ms / 1e3) / 1e12, 2),
+                    "c_identical_all_ranks": bool(same[2].item()),
+                    "multicast_store_bytes_per_rank": GEMM_M * (GEMM_N // world) * 4,
+                    "ingress_GB/s_per_rank": round(egress / (mc_ms / 1e3) / 1e9, 1),
+                    "step": "nplk_gemm_allgather with NPLK_GEMM_MULTIMEM_STORES: every rank's C "
+                            "bound to one NVLink multicast object (symmetric memory); the "
+                            "epilogue stores each tile once (multimem.st) and NVSwitch delivers "
+                            "it to all ranks"}
+    else:
+        multimem = {"unavailable": mc_why}
+    # The end-to-end value: the faster fused form whose C is bit-identical on
+    # every rank.
+    best_ms, best_form = fm, "fused (below): every rank holds the whole row-major C"
+    if mc_ms is not None and bool(same[2].item()) and mc_ms < fm:
+        best_ms = mc_ms
+        best_form = "fused.multimem (below): every rank holds the whole row-major C"
     return {"workload": f"npl_matmul fp32 [8192x4096]@[4096x16384] + bias, B/C column-sharded "
                         f"over {world} GPUs",
             "gemm_only_value": round(GEMM_FLOPS / (gm / 1e3) / 1e12, 2),
-            "end_to_end_value": round(GEMM_FLOPS / (fm / 1e3) / 1e12, 2), "unit": "TFLOP/s",
-            "end_to_end": "fused (below): every rank holds the whole row-major C",
+            "end_to_end_value": round(GEMM_FLOPS / (best_ms / 1e3) / 1e12, 2), "unit": "TFLOP/s",
+            "end_to_end": best_form,
             "gemm_ms": round(gm, 4),
             "nccl": {"gemm_allgather_relayout_ms": round(tm, 4),
                      "c_identical_all_ranks": bool(same[1].item()),
@@ -1268,6 +1304,7 @@ def gemm_dist(args, rank, world, local_rank):
                       "step": "nplk_gemm_allgather: the GEMM epilogue stores every tile into "
                               "all ranks' C over NVLink (CUDA IPC peer pointers) with 16-byte "
                               "stores from its threads",
+                      "multimem": multimem,
                       "tma_stores": {"ms": round(tma_ms, 4),
                                      "value": round(GEMM_FLOPS / (tma_ms / 1e3) / 1e12, 2),
                                      "step": "the same with one TMA tensor store per 32x32 piece "

@@ -65,6 +65,15 @@ extern "C" {
  * measured slower on 2 and 8 B200s (8192 x 16384 x 4096 column-sharded:
  * 1.094 vs 1.031 ms at 8 GPUs). */
 #define NPLK_GEMM_PEER_TMA_STORES 8u
+/* nplk_gemm_allgather: dst[0] (n_dst == 1) is this rank's C as seen through
+ * an NVLink multicast object that binds every rank's C (for example the
+ * multicast address of a symmetric-memory buffer): the epilogue writes each
+ * output element once with a 16-byte multimem store and the NVSwitch delivers
+ * it to every rank's C, so a rank's NVLink egress is its own block once
+ * instead of once per peer. Requires dst[0] 16-byte aligned, ldc, N_local and
+ * col_offset multiples of 4, and not NPLK_GEMM_PEER_TMA_STORES; otherwise the
+ * call returns NPL_ERR_INVALID_ARG. */
+#define NPLK_GEMM_MULTIMEM_STORES 16u
 
 /* ---- dense contractions (tcgen05, 3xTF32) ---------------------------------- */
 
@@ -334,7 +343,9 @@ NPL_API int nplk_ipc_close_handle(void *dev_ptr, uint64_t offset);
  * same C. The epilogue stages each warp's 32 x 32 piece in shared memory and
  * stores it to every destination with 16-byte stores that cover whole
  * 128-byte row segments (NPLK_GEMM_PEER_TMA_STORES: one TMA tensor store per
- * piece and destination instead). beta is 0 (C is not read); other arguments as nplk_gemm. */
+ * piece and destination instead; NPLK_GEMM_MULTIMEM_STORES: one multicast
+ * store per element into the single destination). beta is 0 (C is not read);
+ * other arguments as nplk_gemm. */
 NPL_API int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int64_t K,
                                 float alpha, const float *A, int64_t lda, const float *B,
                                 int64_t ldb, const float *bias, int act, float act_alpha,

@@ -89,6 +89,7 @@ struct GemmDst {
   int n_dst;
   int dst_vec;  // 16-byte stores allowed into every dst
   int rot;      // first destination this rank visits (then in turn, each warp offset by one)
+  int multimem; // dst[0] is a multicast address: one multimem.st reaches every rank's C
   int64_t dst_col;
 };
 struct GemmNoDst {};
@@ -222,7 +223,11 @@ __device__ __forceinline__ void gemm_epilogue_tile(const GemmParams &p, const Ds
             // of all converging on the same peer at the same time.
             int d = pd.rot + (threadIdx.x >> 5);
             while (d >= pd.n_dst) d -= pd.n_dst;
-            if (pd.dst_vec && col + 4 <= p.N) {
+            if (pd.multimem) {
+              // Written once; NVSwitch delivers it to every rank's C (the
+              // host admits this form only with 16-byte aligned whole rows).
+              multimem_st_v4(pd.dst[0] + off, val);
+            } else if (pd.dst_vec && col + 4 <= p.N) {
               for (int i = 0; i < pd.n_dst; ++i) {
                 *reinterpret_cast<float4 *>(pd.dst[d] + off) = val;
                 if (++d == pd.n_dst) d = 0;
@@ -472,6 +477,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     // Every tensor store of this warp complete before the CTA exits.
     if (kTmaDst && lane == 0) bulk_wait_group<0>();
+    if constexpr (std::is_same<Dst, GemmDst>::value) {
+      if (pd.multimem) fence_multimem_release();
+    }
   }
 
   __syncthreads();
@@ -679,6 +687,9 @@ __global__ void __launch_bounds__(kRawThreads, 1)
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+    if constexpr (std::is_same<Dst, GemmDst>::value) {
+      if (pd.multimem) fence_multimem_release();
     }
   } else {
     // ---------------- converters (warps 6..9) ----------------
@@ -984,6 +995,14 @@ extern "C" int nplk_gemm_allgather(void *stream, int64_t M, int64_t N_local, int
     vec = vec && (reinterpret_cast<uintptr_t>(dst[d]) & 15u) == 0;
   }
   pd.dst_vec = vec ? 1 : 0;
+  if (flags & NPLK_GEMM_MULTIMEM_STORES) {
+    // One multicast destination, written with 16-byte multimem stores only.
+    if (n_dst != 1 || !vec || (flags & NPLK_GEMM_PEER_TMA_STORES)) return kErrInvalidArg;
+    pd.multimem = 1;
+    pd.rot = 0;
+    return gemm_run(static_cast<cudaStream_t>(stream), M, N_local, K, A, lda, B, ldb, prm, &pd,
+                    flags, workspace, workspace_bytes, status);
+  }
   // TMA-store form on request, when the destinations allow 16-byte aligned
   // tensor maps and the split operand form runs (a workspace, not forced raw).
   const bool tma = vec && (flags & NPLK_GEMM_PEER_TMA_STORES) &&

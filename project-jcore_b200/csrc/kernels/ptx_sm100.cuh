@@ -183,6 +183,24 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 }
 
 // ---------------------------------------------------------------------------
+// NVLink multicast (NVSwitch fan-out). `mc` is an address inside a multicast
+// object's mapping; one store reaches the same offset of every GPU's memory
+// bound to the object. 16-byte aligned.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void multimem_st_v4(float *mc, float4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// Orders this thread's accesses made through different virtual addresses of
+// the same memory (a multicast address and the unicast one), then makes its
+// writes visible system-wide (other GPUs, the host).
+__device__ __forceinline__ void fence_multimem_release() {
+  asm volatile("fence.proxy.alias;" ::: "memory");
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Programmatic dependent launch: a kernel launched with programmatic stream
 // serialization may start while the previous kernel in the stream still
 // runs; griddep_wait() blocks until that kernel has completed and its

@@ -39,6 +39,7 @@ NPLK_GEMM_TF32_FAST = 1
 NPLK_GEMM_SPLIT_OPERANDS = 2
 NPLK_GEMM_RAW_OPERANDS = 4
 NPLK_GEMM_PEER_TMA_STORES = 8
+NPLK_GEMM_MULTIMEM_STORES = 16
 NPLK_DEBUG_GEMM, NPLK_DEBUG_CONV_WINDOW = 1, 2
 NPLK_STATUS_TIMEOUT_MMA = 102
 

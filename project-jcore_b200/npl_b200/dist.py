@@ -8,7 +8,9 @@ Two partitionings, following the reference's workloads:
     Fused form (``PeerBuffers`` + ``column_sharded_gemm_fused``): every rank
     holds a full row-major C whose address the others map (CUDA IPC), and the
     GEMM's epilogue stores each output tile into all ranks' C over NVLink
-    (nplk_gemm_allgather) -- no separate collective, no relayout. Unfused form
+    (nplk_gemm_allgather) -- no separate collective, no relayout; with
+    ``MulticastBuffers`` instead, every C is bound to one NVLink multicast
+    object and the epilogue stores each tile once for all ranks. Unfused form
     (``column_sharded_gemm``): the blocks are all-gathered ([g][M][N/g], one
     NCCL collective) and rewritten to row-major [M][N] by the relayout kernel.
 """
@@ -171,11 +173,84 @@ class PeerBuffers:
         dist.barrier(group=self.group)
 
 
-def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=None,
+class MulticastBuffers:
+    """Every rank's C bound to one NVLink multicast object.
+
+    Collective: all ranks construct it together with the same shape. Each
+    rank's C is allocated in symmetric memory (torch.distributed's
+    symmetric-memory allocator, outside its pool, so that every C starts its
+    own allocation) and the allocations are bound to one multicast object at
+    the rendezvous. ``ptrs == [mc_ptr]``: this rank's C as seen through the
+    multicast mapping, where one store reaches the same element of every
+    rank's C (NVSwitch fan-out); ``tensor`` is this rank's C for reading.
+    Raises RuntimeError, on every rank, when a GPU or the fabric offers no
+    multicast. close() -- also collective -- releases the mapping after every
+    rank is done with it; no rank may exit or fail while another rank's
+    kernel still stores through it."""
+
+    store_flags = 16  # NPLK_GEMM_MULTIMEM_STORES
+
+    def __init__(self, shape, world: int, rank: int, group=None, device=None):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from torch._C._autograd import DeviceType
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from . import load
+
+        self.lib = load()
+        self.world, self.rank, self.group = world, rank, group
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        ok = bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, dev.index))
+        self._all_or_raise(ok, "NVLink multicast is not supported on this GPU or fabric")
+        size = tuple(int(d) for d in shape)
+        stride = torch._prims_common.make_contiguous_strides_for(size)
+        self.tensor = _SymmetricMemory.empty_strided_p2p(size, stride, torch.float32, dev)
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm_mem.rendezvous(self.tensor, grp)
+        mc = int(self.handle.multicast_ptr or 0)
+        # The multicast address is that of the allocation; C starts it.
+        good = mc != 0 and int(self.handle.offset) == 0 and mc % 16 == 0
+        try:
+            self._all_or_raise(good, "no multicast mapping of C after the rendezvous")
+        except RuntimeError:
+            self.handle = None
+            self.tensor = None
+            raise
+        self.mc_ptr = mc
+        self.ptrs = [mc]
+        torch.cuda.synchronize(dev)
+
+    def _all_or_raise(self, ok: bool, why: str):
+        import torch.distributed as dist
+
+        flags = [None] * self.world
+        dist.all_gather_object(flags, bool(ok), group=self.group)
+        if not all(flags):
+            raise RuntimeError(f"MulticastBuffers: {why} (ranks: {flags})")
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank still stores through the mapping
+        self.handle = None
+        self.tensor = None
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+
+def column_sharded_gemm_fused(A, B, peers, bias=None, workspace=None,
                               act: int = 0, barrier_before: bool = False, flags: int = 0):
     """C = act(A @ B + bias) with B column-sharded, written by every rank
     straight into every rank's C (``peers.tensor``, row-major [M][N]) by the
-    GEMM epilogue (nplk_gemm_allgather). Asynchronous on the current stream.
+    GEMM epilogue (nplk_gemm_allgather). ``peers`` is a PeerBuffers (the
+    epilogue stores each tile into every rank's C over NVLink) or a
+    MulticastBuffers (it stores each tile once through the multicast mapping
+    and NVSwitch delivers it to every rank). Asynchronous on the current
+    stream.
 
     Two orderings are the caller's to keep, because peers store straight into
     this rank's C:
@@ -206,11 +281,12 @@ def column_sharded_gemm_fused(A, B, peers: PeerBuffers, bias=None, workspace=Non
     if workspace is None or workspace.numel() * 4 < ws:
         workspace = torch.empty(ws // 4 + 64, dtype=torch.float32, device=A.device)
     stream = C.c_void_p(torch.cuda.current_stream(A.device).cuda_stream)
-    dst = (C.c_void_p * peers.world)(*peers.ptrs)
+    dst = (C.c_void_p * len(peers.ptrs))(*peers.ptrs)
+    flags |= getattr(peers, "store_flags", 0)
     b_ptr = B.data_ptr() + c0 * B.element_size()
     bias_ptr = C.c_void_p(bias.data_ptr() + c0 * bias.element_size()) if bias is not None else None
     rc = lib.nplk_gemm_allgather(stream, M, w, K, 1.0, C.c_void_p(A.data_ptr()), K,
-                                 C.c_void_p(b_ptr), N, bias_ptr, act, 0.0, dst, peers.world, c0,
+                                 C.c_void_p(b_ptr), N, bias_ptr, act, 0.0, dst, len(peers.ptrs), c0,
                                  N, flags, C.c_void_p(workspace.data_ptr()), ws, None)
     if rc != 0:
         raise RuntimeError(f"nplk_gemm_allgather failed: {rc}")

@@ -167,9 +167,9 @@ def test_multi_gpu_entry_points_argument_checks(lib):
 
     fake = C.c_void_p(0x1000)  # never dereferenced: every call below fails its checks
 
-    def allgather(dst, n_dst, col_offset, ldc, n_local=64):
+    def allgather(dst, n_dst, col_offset, ldc, n_local=64, flags=0):
         return lib.nplk_gemm_allgather(None, 128, n_local, 64, 1.0, fake, 64, fake, 128, None, 0,
-                                       0.0, dst, n_dst, col_offset, ldc, 0, None, 0, None)
+                                       0.0, dst, n_dst, col_offset, ldc, flags, None, 0, None)
 
     two = (C.c_void_p * 2)(0x1000, 0x2000)
     nine = (C.c_void_p * 9)(*([0x1000] * 9))
@@ -180,6 +180,18 @@ def test_multi_gpu_entry_points_argument_checks(lib):
     assert allgather(two, 2, -4, 128) == nb.NPL_ERR_INVALID_ARG          # negative column
     assert allgather(two, 2, 96, 128) == nb.NPL_ERR_INVALID_ARG          # block past ldc
     assert allgather(with_null, 2, 0, 128) == nb.NPL_ERR_INVALID_ARG     # a null destination
+    # The multicast form: exactly one 16-byte aligned destination, whole
+    # 16-byte pieces (ldc, N_local, col_offset multiples of 4), no TMA stores.
+    mm = nb.NPLK_GEMM_MULTIMEM_STORES
+    one = (C.c_void_p * 1)(0x1000)
+    odd = (C.c_void_p * 1)(0x1004)
+    assert allgather(two, 2, 0, 128, flags=mm) == nb.NPL_ERR_INVALID_ARG
+    assert allgather(odd, 1, 0, 128, flags=mm) == nb.NPL_ERR_INVALID_ARG
+    assert allgather(one, 1, 2, 128, flags=mm) == nb.NPL_ERR_INVALID_ARG
+    assert allgather(one, 1, 0, 130, flags=mm) == nb.NPL_ERR_INVALID_ARG
+    assert allgather(one, 1, 0, 128, n_local=62, flags=mm) == nb.NPL_ERR_INVALID_ARG
+    assert allgather(one, 1, 0, 128, flags=mm | nb.NPLK_GEMM_PEER_TMA_STORES) == \
+        nb.NPL_ERR_INVALID_ARG
 
 
 def test_fault_injection_hooks_arm_and_disarm(lib):

@@ -151,3 +151,70 @@ def test_gemm_allgather_ipc_two_processes():
     assert sorted(results.keys()) == [0, 1]
     for nan_count, err in results.values():
         assert nan_count == 0 and err < 1e-4
+
+
+def _multicast_rank(rank, world, port, results):
+    import os
+    import torch
+    import torch.distributed as dist
+    from npl_b200 import dist as nd
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.cuda.set_device(rank)
+        gen = torch.Generator(device="cuda").manual_seed(0)  # the same A, B on every rank
+        M, K, N = 384, 200, world * 136
+        A = torch.randn(M, K, device="cuda", generator=gen)
+        B = torch.randn(K, N, device="cuda", generator=gen) / 10.0
+        bias = torch.randn(N, device="cuda", generator=gen) * 0.1
+        full = torch.full((M, N), float("nan"), device="cuda")
+        peers = nd.PeerBuffers(full, world, rank)
+        nd.column_sharded_gemm_fused(A, B, peers, bias, act=1)
+        torch.cuda.synchronize()
+        dist.barrier()
+        peers.close()
+        mc = nd.MulticastBuffers((M, N), world, rank)
+        got = []
+        try:  # every rank releases the mapping together, also on an error
+            mc.tensor.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            for _ in range(2):  # two calls in a row, same result
+                nd.column_sharded_gemm_fused(A, B, mc, bias, act=1, barrier_before=True)
+                torch.cuda.synchronize()
+                dist.barrier()  # every rank's multicast stores have landed in every C
+                got.append(mc.tensor.cpu().numpy())
+        finally:
+            mc.close()
+        ref = np.maximum(A.double().cpu().numpy() @ B.double().cpu().numpy()
+                         + bias.double().cpu().numpy(), 0.0)
+        ipc = full.cpu().numpy()
+        results[rank] = (float(np.isnan(got[1]).sum()), S.normwise_err(got[1], ref),
+                         bool(np.array_equal(got[0], ipc) and np.array_equal(got[1], ipc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gemm_allgather_multicast_two_gpus():
+    # Two ranks on two GPUs: every rank's C bound to one NVLink multicast
+    # object; each rank's GEMM epilogue stores its block once (multimem.st)
+    # and both ranks end with the whole C, bit-identical to the peer-store
+    # form. Needs two GPUs with NVLink multicast.
+    import torch
+    import torch.multiprocessing as mp
+    from torch._C._autograd import DeviceType
+    from torch._C._distributed_c10d import _SymmetricMemory
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if not all(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, d) for d in (0, 1)):
+        pytest.skip("no NVLink multicast on these GPUs")
+    world = 2
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_multicast_rank, args=(world, _free_port(), results), nprocs=world,
+                       start_method="spawn", join=True)
+    assert sorted(results.keys()) == [0, 1]
+    for nan_count, err, same_as_ipc in results.values():
+        assert nan_count == 0 and err < 1e-4 and same_as_ipc
+
