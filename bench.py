@@ -1141,9 +1141,12 @@ def gemm_dist(args, rank, world, local_rank):
     """Column-sharded large GEMM on `world` GPUs: each rank computes its block
     of C = A @ B + bias (A replicated) and every rank ends with the whole
     row-major C, either through the fused GEMM whose epilogue stores each tile
-    into all ranks' C over NVLink (the end-to-end value) or through the GEMM
-    followed by an NCCL all-gather and the relayout kernel. Device time per
-    step, max over ranks, for the GEMM alone and for each form."""
+    into all ranks' C over NVLink (peer stores from its threads or the TMA
+    unit, or one store through an NVLink multicast object where the fabric
+    offers multicast; the faster bit-identical fused form is the end-to-end
+    value) or through the GEMM followed by an NCCL all-gather and the relayout
+    kernel. Device time per step, max over ranks, for the GEMM alone and for
+    each form."""
     import torch
     import torch.distributed as dist
     from npl_b200 import dist as nd
